@@ -1,0 +1,364 @@
+#!/usr/bin/env python
+"""Benchmark of the W4A16 GEMV hot path on B200 (one JSON line on rank 0).
+
+Workload (BASELINE metric "W4A16 GEMV us & HBM GB/s at 4096x4096, streaming"):
+  int4gemv N=K=4096, G=128, W ~ N(0, 0.02^2) quantised offline, x ~ N(0,1);
+  a pool of 64 independently seeded weight sets (64 x 8.67 MB = 555 MB, far
+  above the 126 MB L2) and 64 x / y buffers, cycled launch by launch, so every
+  launch streams its weights from HBM.  One step = one pass over the pool (64
+  GEMVs), captured once in a CUDA graph with programmatic dependent launch
+  between consecutive GEMVs and replayed.
+
+value   = algorithmic bytes moved by all ranks / max-over-ranks device time
+          (GB/s; bytes per GEMV = N*K/2 + N*K/64 + 2K + 2N = 8,667,136).
+e2e     = same metric through the public API (ext.forward_into via the C ABI)
+          with x copied host->device from pinned memory and y copied back for
+          every GEMV, wall clock around the steps, weights resident.
+--gpus N under torchrun: every rank runs its own pool (weak scaling, no
+data-path collective); only the timing reduction uses NCCL.
+--impl reference: the reference's CPU path (dequantise to fp32, then fp32 mv)
+restated in C (oracle/cpu_gemv.c), all host threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_ROWS = 4096
+K_COLS = 4096
+POOL = 64
+METRIC = "W4A16 GEMV us & HBM GB/s (% of ~8 TB/s) at 4096x4096, streaming mode"
+NOMINAL_HBM_GBS = 8000.0
+
+
+def algo_bytes(N=N_ROWS, K=K_COLS):
+    return N * K // 2 + N * (K // 128) * 2 + 2 * K + 2 * N
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic(variant: str):
+    """dram bytes per launch of `variant` on this workload from the committed
+    ncu summary (profiles/<variant>_int4_4096x4096.md, line 'traffic_bytes_per_launch: B')."""
+    f = ROOT / "profiles" / f"{variant}_int4_4096x4096.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons on one GPU."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(self.idx), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.perf_counter(), line.strip()))
+
+    def mark(self, which):
+        setattr(self, which, time.perf_counter())
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for t, line in self.samples:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((t, float(parts[0]), float(parts[1]), parts))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        inside = [r for r in rows if self.t0 and self.t1 and self.t0 <= r[0] <= self.t1]
+        use = inside or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in use for i in range(4)
+                          if r[3][4 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[1] for r in use),
+                "sm_max_mhz": max(r[2] for r in use), "reasons": reasons,
+                "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+def run_reference(args):
+    """CPU arm: the reference's dequantise-then-mv path on the host cores."""
+    import numpy as np
+    from oracle import cpu_gemv
+    from cudalab_b200.operators.int4gemv import make_w4, make_x4
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = cpu_gemv.max_threads()
+    Wp, s16, _ = make_w4(N_ROWS, K_COLS, seed=1234 + 100000, scale=0.02, device="cpu")
+    x = make_x4(K_COLS, seed=1234, device="cpu")
+    Wp_n, s_n, x_n = Wp.numpy(), s16.numpy().view(np.uint16), x.numpy().view(np.uint16)
+    ws = cpu_gemv.Workspace(N_ROWS, K_COLS)
+    t = time.perf_counter()
+    cpu_gemv.int4_gemv(Wp_n, s_n, x_n, threads, ws)
+    t_full = time.perf_counter() - t
+    # bounded sample: rows per step so that the whole run stays near a minute
+    budget = 60.0
+    steps_total = args.steps + args.warmup
+    rows = N_ROWS if steps_total * t_full <= budget else \
+        max(64, int(N_ROWS * budget / (steps_total * t_full)) // 64 * 64)
+    Wp_s, s_s = np.ascontiguousarray(Wp_n[:rows]), np.ascontiguousarray(s_n[:rows])
+    ws_s = cpu_gemv.Workspace(rows, K_COLS)
+    for _ in range(args.warmup):
+        cpu_gemv.int4_gemv(Wp_s, s_s, x_n, threads, ws_s)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_gemv.int4_gemv(Wp_s, s_s, x_n, threads, ws_s)
+    dt = time.perf_counter() - t0
+    bytes_step = algo_bytes(rows, K_COLS)
+    gbs = bytes_step * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8 nibbles -> fp32 acc",
+        "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x)",
+        "config": {"workload": f"int4gemv {rows}x{K_COLS} rows of the 4096x4096 W4A16 GEMV "
+                               "(dequantise to fp32, fp32 mv, fp16 out) on host cores",
+                   "N": rows, "K": K_COLS, "group": 128},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{args.steps} steps x {rows} rows of 4096x4096 "
+                                   f"(full 4096-row GEMV {t_full * 1e3:.1f} ms)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "us_per_gemv_4096": round(t_full * 1e6, 1),
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def cpu_baseline_sample():
+    """Bounded (~10 s) timing of the CPU restatement on the same workload."""
+    import numpy as np
+    from oracle import cpu_gemv
+    from cudalab_b200.operators.int4gemv import make_w4, make_x4
+    threads = cpu_gemv.max_threads()
+    Wp, s16, _ = make_w4(N_ROWS, K_COLS, seed=1234 + 100000, scale=0.02, device="cpu")
+    x = make_x4(K_COLS, seed=1234, device="cpu")
+    Wp_n, s_n, x_n = Wp.numpy(), s16.numpy().view(np.uint16), x.numpy().view(np.uint16)
+    ws = cpu_gemv.Workspace(N_ROWS, K_COLS)
+    cpu_gemv.int4_gemv(Wp_n, s_n, x_n, threads, ws)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0 or n < 3:
+        cpu_gemv.int4_gemv(Wp_n, s_n, x_n, threads, ws)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(algo_bytes() / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} full 4096x4096 GEMVs (dequantise to fp32 + fp32 mv), "
+                      f"{dt * 1e3:.2f} ms each, ~10 s total"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=100)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--variant", default="int4gemv_bulk")
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from cudalab_b200 import _native as nat
+    from cudalab_b200.build import build
+    from cudalab_b200.operators.int4gemv import int4gemv as op
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    ext = build("int4gemv")
+    flags = 0 if args.no_pdl else nat.CL_LAUNCH_PDL
+    pool = op.make_bench_pool(N_ROWS, K_COLS, mode="l2cold", pool_size=POOL, weight_dist=0.02)
+
+    # ---- capture one pass over the pool ----
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for i in range(POOL):
+            pool.launch(ext, args.variant, i, flags=flags)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(POOL):
+            pool.launch(ext, args.variant, i, flags=flags)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            g.replay()
+    barrier()
+    sampler = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    sampler.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    sampler.mark("t0")
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(s)
+    barrier()
+    sampler.mark("t1")
+    ms = e0.elapsed_time(e1)
+    time.sleep(0.25)
+    sampler.stop()
+    status = nat.device_status(clear=True)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    launches = args.steps * POOL
+    us_per_gemv = ms * 1e3 / launches
+    bytes_per = algo_bytes()
+    value = bytes_per * launches * world / (ms * 1e-3) / 1e9
+    achieved = bytes_per / (us_per_gemv * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+
+    # ---- e2e through the public API: pinned x H2D, forward_into, y D2H ----
+    xs_h = [x.cpu().pin_memory() for x in pool.xs]
+    ys_h = [torch.empty(N_ROWS, dtype=torch.float16).pin_memory() for _ in pool.xs]
+    weights = pool.shared["weights"]
+
+    def e2e_step():
+        with torch.cuda.stream(s):
+            for i in range(POOL):
+                pool.xs[i].copy_(xs_h[i], non_blocking=True)
+                Wp, sc = weights[i]
+                ext.forward_into(args.variant, Wp, sc, pool.xs[i], pool.outs[i])
+                ys_h[i].copy_(pool.outs[i], non_blocking=True)
+        s.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_val = bytes_per * POOL * args.e2e_steps * world / e2e_s / 1e9
+
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu_base = cpu_baseline_sample()
+        except Exception as exc:  # noqa: BLE001
+            cpu_base = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+
+    traffic = committed_traffic(args.variant)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 (u8 nibbles) x fp16 -> fp32 acc",
+            "data": "synthetic: seeded W ~ N(0,0.02^2) quantised G=128, x ~ N(0,1)",
+            "config": {"workload": "int4gemv W4A16 4096x4096 G=128, L2-cold pool of 64 weight "
+                                   "sets (555 MB, inputs larger than L2), 64 GEMVs per step, "
+                                   "CUDA graph" + ("" if args.no_pdl else " + PDL"),
+                       "N": N_ROWS, "K": K_COLS, "pool": POOL, "variant": args.variant,
+                       "l2": "inputs larger than L2 (pool cycled)",
+                       "parallelism": f"replicas x{world}"},
+            "us_per_gemv": round(us_per_gemv, 4),
+            "pct_of_nominal_8TBs": round(100 * achieved / NOMINAL_HBM_GBS, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind,
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": bytes_per},
+            "cpu_baseline": cpu_base,
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": POOL * K_COLS * 2,
+                    "d2h_bytes_per_step": POOL * N_ROWS * 2,
+                    "us_per_gemv": round(e2e_s * 1e6 / (POOL * args.e2e_steps), 2),
+                    "note": "public API (forward_into over the C ABI) per GEMV: pinned x H2D, "
+                            "launch, y D2H; wall clock; weights resident"},
+            "gpu_launches": launches,
+            "device_status": status,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line))
+    del g
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

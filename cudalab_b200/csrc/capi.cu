@@ -1,0 +1,219 @@
+// C ABI of libcudalab_gemv.so (declarations: include/cudalab_gemv.h).
+//
+// Plain pointers and sizes only.  This layer owns: the variant registry
+// lookup, the pointer/size contract checks that do not need tensor metadata,
+// status codes + a per-thread error message, and the native launch-loop timer.
+// Tensor-level checks (dims, dtypes, devices, contiguity) are made by the host
+// wrapper before the call, in the order of the reference extension.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/cudalab_gemv.h"
+#include "gemv_launch.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(CL_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                                 cudaGetErrorString(e) + ")");
+}
+
+const clb::VariantDesc* find(const clb::VariantDesc* table, int n, const char* name) {
+    if (name == nullptr) return nullptr;
+    for (int i = 0; i < n; ++i)
+        if (std::strcmp(table[i].name, name) == 0) return &table[i];
+    return nullptr;
+}
+
+std::string unknown_msg(const char* op, const clb::VariantDesc* table, int n, const char* name) {
+    std::vector<std::string> names;
+    for (int i = 0; i < n; ++i)
+        if (!table[i].quarantined) names.emplace_back(table[i].name);
+    std::sort(names.begin(), names.end());
+    std::string s = std::string("unknown ") + op + " variant '" + (name ? name : "(null)") +
+                    "'; available: ";
+    for (auto& v : names) s += v + " ";
+    return s;
+}
+
+int list_variants(const clb::VariantDesc* table, int n, int which, char* buf, size_t len,
+                  size_t* needed) {
+    std::vector<std::string> names;
+    for (int i = 0; i < n; ++i) {
+        const bool q = table[i].quarantined;
+        if (which == CL_VARIANTS_NORMAL && q) continue;
+        if (which == CL_VARIANTS_QUARANTINED && !q) continue;
+        names.emplace_back(table[i].name);
+    }
+    std::sort(names.begin(), names.end());
+    std::string joined;
+    for (size_t i = 0; i < names.size(); ++i) {
+        if (i) joined += '\n';
+        joined += names[i];
+    }
+    if (needed) *needed = joined.size() + 1;
+    if (which != CL_VARIANTS_NORMAL && which != CL_VARIANTS_ALL && which != CL_VARIANTS_QUARANTINED)
+        return fail(CL_ERR_INVALID_ARGUMENT, "list_variants: unknown selector");
+    if (buf == nullptr || len < joined.size() + 1)
+        return fail(CL_ERR_BUFFER_TOO_SMALL, "list_variants: buffer too small");
+    std::memcpy(buf, joined.c_str(), joined.size() + 1);
+    return CL_OK;
+}
+
+// Shared argument checks.  is_int4 adds the group-size contract K % 128 == 0.
+int check_args(const char* op, const void* W, const void* scale, const void* x, const void* out,
+               int64_t N, int64_t K, bool is_int4) {
+    if (N <= 0) return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": N must be > 0");
+    if (K <= 0) return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": K must be > 0");
+    if (is_int4 && (K % 128) != 0)
+        return fail(CL_ERR_INVALID_ARGUMENT,
+                    std::string(op) + ": K must be divisible by 128 (group_size=128)");
+    if (N > (int64_t)1 << 31)
+        return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": N exceeds 2^31 rows");
+    if (!W || !scale || !x || !out)
+        return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": null device pointer");
+    return CL_OK;
+}
+
+int run(const clb::VariantDesc* table, int n, const char* op, const char* variant, const void* W,
+        const void* scale, const void* x, void* out, int64_t N, int64_t K, void* stream,
+        uint32_t flags, bool is_int4) {
+    const clb::VariantDesc* v = find(table, n, variant);
+    if (!v) return fail(CL_ERR_UNKNOWN_VARIANT, unknown_msg(op, table, n, variant));
+    const int rc = check_args(op, W, scale, x, out, N, K, is_int4);
+    if (rc != CL_OK) return rc;
+    cudaError_t e = v->fn(W, scale, x, out, N, K, static_cast<cudaStream_t>(stream), flags);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    return CL_OK;
+}
+
+int timing(const clb::VariantDesc* table, int n, const char* op, const char* variant,
+           const void* W, const void* scale, const void* x, void* out, int64_t N, int64_t K,
+           int64_t warmup, int64_t n_windows, int64_t lpw, void* stream_v, uint32_t flags,
+           double* per_window_us, bool is_int4) {
+    const clb::VariantDesc* v = find(table, n, variant);
+    if (!v) return fail(CL_ERR_UNKNOWN_VARIANT, unknown_msg(op, table, n, variant));
+    if (warmup < 0) return fail(CL_ERR_INVALID_ARGUMENT, "warmup must be >= 0");
+    if (n_windows < 1) return fail(CL_ERR_INVALID_ARGUMENT, "n_windows must be >= 1");
+    if (lpw < 1) return fail(CL_ERR_INVALID_ARGUMENT, "launches_per_window must be >= 1");
+    if (!per_window_us) return fail(CL_ERR_INVALID_ARGUMENT, "per_window_us is null");
+    int rc = check_args(op, W, scale, x, out, N, K, is_int4);
+    if (rc != CL_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+    for (int64_t i = 0; i < warmup; ++i) {
+        cudaError_t e = v->fn(W, scale, x, out, N, K, s, flags);
+        if (e != cudaSuccess) return cuda_fail(e, "warmup launch");
+    }
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "warmup synchronize");
+    cudaEvent_t ev0, ev1;
+    if ((e = cudaEventCreate(&ev0)) != cudaSuccess) return cuda_fail(e, "event create");
+    if ((e = cudaEventCreate(&ev1)) != cudaSuccess) {
+        cudaEventDestroy(ev0);
+        return cuda_fail(e, "event create");
+    }
+    rc = CL_OK;
+    for (int64_t w = 0; w < n_windows && rc == CL_OK; ++w) {
+        if ((e = cudaEventRecord(ev0, s)) != cudaSuccess) { rc = cuda_fail(e, "event record"); break; }
+        for (int64_t i = 0; i < lpw; ++i) {
+            e = v->fn(W, scale, x, out, N, K, s, flags);
+            if (e != cudaSuccess) { rc = cuda_fail(e, "timed launch"); break; }
+        }
+        if (rc != CL_OK) break;
+        if ((e = cudaEventRecord(ev1, s)) != cudaSuccess) { rc = cuda_fail(e, "event record"); break; }
+        if ((e = cudaEventSynchronize(ev1)) != cudaSuccess) { rc = cuda_fail(e, "event sync"); break; }
+        float ms = 0.f;
+        if ((e = cudaEventElapsedTime(&ms, ev0, ev1)) != cudaSuccess) { rc = cuda_fail(e, "elapsed"); break; }
+        per_window_us[w] = (double)ms * 1e3 / (double)lpw;
+    }
+    cudaEventDestroy(ev0);
+    cudaEventDestroy(ev1);
+    return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cl_version(void) { return "cudalab-b200 0.1.0 (sm_100a)"; }
+
+const char* cl_last_error(void) { return g_last_error.c_str(); }
+
+int cl_device_status(int clear, int* status_out) {
+    if (!status_out) return fail(CL_ERR_INVALID_ARGUMENT, "status_out is null");
+    cudaError_t e = clb::read_device_status(clear, status_out);
+    if (e != cudaSuccess) return cuda_fail(e, "read device status");
+    return CL_OK;
+}
+
+// ---- INT4 ----
+int cl_int4gemv_ex(const char* variant, const uint8_t* W_packed, const void* scale, const void* x,
+                   void* out, int64_t N, int64_t K, void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int4_variants(&n);
+    return run(t, n, "int4gemv", variant, W_packed, scale, x, out, N, K, stream, flags, true);
+}
+
+int cl_int4gemv(const char* variant, const uint8_t* W_packed, const void* scale, const void* x,
+                void* out, int64_t N, int64_t K, void* stream) {
+    return cl_int4gemv_ex(variant, W_packed, scale, x, out, N, K, stream, 0u);
+}
+
+int cl_int4gemv_native_timing(const char* variant, const uint8_t* W_packed, const void* scale,
+                              const void* x, void* out, int64_t N, int64_t K, int64_t warmup,
+                              int64_t n_windows, int64_t launches_per_window, void* stream,
+                              uint32_t flags, double* per_window_us) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int4_variants(&n);
+    return timing(t, n, "int4gemv", variant, W_packed, scale, x, out, N, K, warmup, n_windows,
+                  launches_per_window, stream, flags, per_window_us, true);
+}
+
+int cl_int4gemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int4_variants(&n);
+    return list_variants(t, n, which, buf, buf_len, needed);
+}
+
+// ---- INT8 ----
+int cl_qgemv_ex(const char* variant, const int8_t* W_q, const float* scale, const void* x,
+                void* out, int64_t N, int64_t K, void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int8_variants(&n);
+    return run(t, n, "qgemv", variant, W_q, scale, x, out, N, K, stream, flags, false);
+}
+
+int cl_qgemv(const char* variant, const int8_t* W_q, const float* scale, const void* x, void* out,
+             int64_t N, int64_t K, void* stream) {
+    return cl_qgemv_ex(variant, W_q, scale, x, out, N, K, stream, 0u);
+}
+
+int cl_qgemv_native_timing(const char* variant, const int8_t* W_q, const float* scale,
+                           const void* x, void* out, int64_t N, int64_t K, int64_t warmup,
+                           int64_t n_windows, int64_t launches_per_window, void* stream,
+                           uint32_t flags, double* per_window_us) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int8_variants(&n);
+    return timing(t, n, "qgemv", variant, W_q, scale, x, out, N, K, warmup, n_windows,
+                  launches_per_window, stream, flags, per_window_us, false);
+}
+
+int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int8_variants(&n);
+    return list_variants(t, n, which, buf, buf_len, needed);
+}
+
+}  // extern "C"

@@ -1,0 +1,30 @@
+// Internal interface between the kernel translation unit (gemv_kernels.cu)
+// and the C ABI translation unit (capi.cu).  Not installed; the public ABI is
+// include/cudalab_gemv.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace clb {
+
+// Launches one GEMV of a given variant.  W is uint8 (INT4 packed) or int8
+// (INT8); scale is fp16 [N, K/128] (INT4) or fp32 [N] (INT8).  flags are the
+// CL_LAUNCH_* bits of the public header.
+using LaunchFn = cudaError_t (*)(const void* W, const void* scale, const void* x, void* y,
+                                 int64_t N, int64_t K, cudaStream_t stream, unsigned flags);
+
+struct VariantDesc {
+    const char* name;
+    LaunchFn fn;
+    bool quarantined;  // registered but not in the normal dispatch list
+};
+
+const VariantDesc* int4_variants(int* count);
+const VariantDesc* int8_variants(int* count);
+
+// Reads (optionally clears) the device-side bounded-wait status word of the
+// current device.
+cudaError_t read_device_status(int clear, int* status);
+
+}  // namespace clb

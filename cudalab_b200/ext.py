@@ -1,0 +1,247 @@
+"""Host-side operator extensions: the drop-in replacement of the reference's
+per-operator pybind modules.
+
+`Int4gemvExt` mirrors kernels/int4gemv/bindings.cpp (forward :145-159,
+forward_into :163-176, native_timing :180-253, variant lists :258-285) and
+`QgemvExt` mirrors kernels/qgemv/bindings.cpp (:66-115, :281-306).  The
+tensor-metadata checks run here, before any device work, in the reference's
+order (variant lookup, then W: dim -> N>0 -> K>0 -> dtype -> [K%128] ->
+contiguous -> is_cuda, then scale, x, out), and raise RuntimeError whose first
+line carries the same message substring as the reference (its negative suite
+matches those substrings), followed by an English rendering.  The computation
+itself always goes through the C ABI of libcudalab_gemv.so.
+"""
+from __future__ import annotations
+
+import ctypes
+import statistics
+
+import torch
+
+from . import _native as nat
+
+NATIVE_NOTE = ("native kernel-loop timing: back-to-back launches issued from C++, "
+               "CUDA events around each window / launches per window; excludes the "
+               "Python boundary (distinct from the API-path and ncu durations)")
+
+
+def _chk(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream_ptr(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+class _ExtBase:
+    kind = ""          # "int4gemv" | "qgemv"
+    w_name = ""        # "W_packed" | "W_q"
+
+    def __init__(self) -> None:
+        self._lib = nat.load()
+        self._cache = {}
+
+    # ---- variant registry ----
+    def variants(self) -> list[str]:
+        return nat.list_variants(self.kind, nat.CL_VARIANTS_NORMAL)
+
+    def all_variants(self) -> list[str]:
+        return nat.list_variants(self.kind, nat.CL_VARIANTS_ALL)
+
+    def quarantined_variants(self) -> list[str]:
+        return nat.list_variants(self.kind, nat.CL_VARIANTS_QUARANTINED)
+
+    def _check_variant(self, name: str) -> None:
+        allv = self._cache.get("all")
+        if allv is None:
+            allv = self._cache["all"] = set(self.all_variants())
+        if name not in allv:
+            normal = " ".join(self.variants())
+            raise RuntimeError(f"未知 {self.kind} 变体 '{name}'。正常可用: {normal} "
+                               f"(unknown {self.kind} variant)")
+
+    # ---- shared checks on x / out (reference order: dim, size, dtype,
+    #      contiguous, is_cuda, same device) ----
+    def _validate_x(self, W: torch.Tensor, x: torch.Tensor, K: int) -> None:
+        _chk(x.dim() == 1, f"x 必须是 1 维 (K,)，实际 {x.dim()} 维 (x must be 1-D)")
+        _chk(x.size(0) == K, f"x 长度必须等于 K: x={x.size(0)} K={K} (len(x) must equal K)")
+        _chk(x.dtype == torch.float16,
+             f"x 必须是 float16（FP16 activation）, 实际 {x.dtype} (x must be float16)")
+        _chk(x.is_contiguous(), "x 必须是连续内存 (x must be contiguous)")
+        _chk(x.is_cuda, "x 必须是 CUDA 张量 (x must be a CUDA tensor)")
+        _chk(x.device == W.device,
+             f"x 必须与 {self.w_name} 在同一 CUDA 设备上 (x must be on the device of "
+             f"{self.w_name})")
+
+    def _validate_out(self, W: torch.Tensor, out: torch.Tensor) -> None:
+        N = W.size(0)
+        _chk(out.dim() == 1, f"out 必须是 1 维 (N,)，实际 {out.dim()} 维 (out must be 1-D)")
+        _chk(out.size(0) == N,
+             f"out 长度必须等于 N: out={out.size(0)} N={N} (len(out) must equal N)")
+        _chk(out.dtype == torch.float16,
+             f"out 必须是 float16，实际 {out.dtype} (out must be float16)")
+        _chk(out.is_contiguous(), "out 必须是连续内存 (out must be contiguous)")
+        _chk(out.is_cuda, "out 必须是 CUDA 张量 (out must be a CUDA tensor)")
+        _chk(out.device == W.device,
+             f"out 必须与 {self.w_name} 在同一 CUDA 设备上 (out must be on the device of "
+             f"{self.w_name})")
+
+    # subclasses: _validate_w, _validate_scale, _k_of, _call
+    def _validate_inputs(self, W, scale, x) -> int:
+        self._validate_w(W)
+        self._validate_scale(W, scale)
+        K = self._k_of(W)
+        self._validate_x(W, x, K)
+        return K
+
+    def _launch(self, name: str, W, scale, x, out, flags: int = 0) -> None:
+        N, K = W.size(0), self._k_of(W)
+        dev = W.device
+        with torch.cuda.device(dev):
+            rc = self._call(name.encode(), W.data_ptr(), scale.data_ptr(), x.data_ptr(),
+                            out.data_ptr(), N, K, _stream_ptr(dev), flags)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"{self.kind} launch failed ({rc}): {nat.last_error(self._lib)}")
+
+    # ---- public API (names and keyword names of the reference module) ----
+    def forward(self, variant: str, W, scale, x, flags: int = 0) -> torch.Tensor:
+        self._check_variant(variant)
+        self._validate_inputs(W, scale, x)
+        out = torch.empty(W.size(0), dtype=torch.float16, device=W.device)
+        self._launch(variant, W, scale, x, out, flags)
+        return out
+
+    def forward_into(self, variant: str, W, scale, x, out, flags: int = 0) -> None:
+        self._check_variant(variant)
+        self._validate_inputs(W, scale, x)
+        self._validate_out(W, out)
+        self._launch(variant, W, scale, x, out, flags)
+
+    def native_timing(self, variant: str, W, scale, x, out, warmup: int = 200,
+                      n_windows: int = 10, launches_per_window: int = 64,
+                      flags: int = 0) -> dict:
+        self._check_variant(variant)
+        _chk(warmup >= 0, f"warmup 必须 >= 0，实际 {warmup} (warmup must be >= 0)")
+        _chk(n_windows >= 1, f"n_windows 必须 >= 1，实际 {n_windows} (n_windows must be >= 1)")
+        _chk(launches_per_window >= 1,
+             f"launches_per_window 必须 >= 1，实际 {launches_per_window} "
+             "(launches_per_window must be >= 1)")
+        self._validate_inputs(W, scale, x)
+        self._validate_out(W, out)
+        N, K = W.size(0), self._k_of(W)
+        buf = (ctypes.c_double * n_windows)()
+        dev = W.device
+        with torch.cuda.device(dev):
+            rc = self._timing(variant.encode(), W.data_ptr(), scale.data_ptr(), x.data_ptr(),
+                              out.data_ptr(), N, K, warmup, n_windows, launches_per_window,
+                              _stream_ptr(dev), flags, buf)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"native_timing failed ({rc}): {nat.last_error(self._lib)}")
+        per = [float(v) for v in buf]
+        s = sorted(per)
+        return {
+            "variant": variant,
+            "warmup": warmup,
+            "n_windows": n_windows,
+            "launches_per_window": launches_per_window,
+            "window_median_us": per,
+            "median_us": statistics.median(s),
+            "min_us": s[0],
+            "max_us": s[-1],
+            "mean_us": sum(s) / len(s),
+            "note": NATIVE_NOTE,
+        }
+
+
+class Int4gemvExt(_ExtBase):
+    """W4A16: W_packed uint8 [N, K/2], scale fp16 [N, K/128], x fp16 [K]."""
+    kind = "int4gemv"
+    w_name = "W_packed"
+
+    def __init__(self) -> None:
+        super().__init__()
+        self._call = self._lib.cl_int4gemv_ex
+        self._timing = self._lib.cl_int4gemv_native_timing
+
+    def _k_of(self, W) -> int:
+        return 2 * W.size(1)
+
+    def _validate_w(self, Wp: torch.Tensor) -> None:
+        _chk(Wp.dim() == 2, f"W_packed 必须是 2 维 (N, K/2)，实际 {Wp.dim()} 维 "
+                            "(W_packed must be 2-D)")
+        _chk(Wp.size(0) > 0, f"N 必须 > 0，实际 {Wp.size(0)} (N must be > 0)")
+        _chk(Wp.size(1) > 0, f"K/2 必须 > 0，实际 {Wp.size(1)} (K/2 must be > 0)")
+        _chk(Wp.dtype == torch.uint8,
+             f"W_packed 必须是 uint8（torch uint8 为 kByte），实际 {Wp.dtype} "
+             "(W_packed must be uint8)")
+        K = 2 * Wp.size(1)
+        _chk(K % 128 == 0, f"K 必须可被 128 整除（group_size=128 合同）, 实际 K={K} "
+                           "(K must be divisible by 128)")
+        _chk(Wp.is_contiguous(), "W_packed 必须是连续内存 (W_packed must be contiguous)")
+        _chk(Wp.is_cuda, "W_packed 必须是 CUDA 张量 (W_packed must be a CUDA tensor)")
+
+    def _validate_scale(self, Wp: torch.Tensor, scale: torch.Tensor) -> None:
+        N, K = Wp.size(0), 2 * Wp.size(1)
+        _chk(scale.dim() == 2, f"scale 必须是 2 维 (N, K/128)，实际 {scale.dim()} 维 "
+                               "(scale must be 2-D)")
+        _chk(scale.size(0) == N, f"scale 行数必须等于 N: scale={scale.size(0)} N={N} "
+                                 "(scale rows must equal N)")
+        _chk(scale.size(1) == K // 128,
+             f"scale 组数必须等于 K/128（invalid group count）: scale={scale.size(1)} "
+             f"K/128={K // 128} (scale groups must equal K/128)")
+        _chk(scale.dtype == torch.float16,
+             f"scale 必须是 float16（group-wise 合同）, 实际 {scale.dtype} "
+             "(scale must be float16)")
+        _chk(scale.is_contiguous(), "scale 必须是连续内存 (scale must be contiguous)")
+        _chk(scale.is_cuda, "scale 必须是 CUDA 张量 (scale must be a CUDA tensor)")
+        _chk(scale.device == Wp.device,
+             "scale 必须与 W_packed 在同一 CUDA 设备上 (scale must be on the device of W_packed)")
+
+
+class QgemvExt(_ExtBase):
+    """INT8: W_q int8 [N, K], scale fp32 [N], x fp16 [K]."""
+    kind = "qgemv"
+    w_name = "W_q"
+
+    def __init__(self) -> None:
+        super().__init__()
+        self._call = self._lib.cl_qgemv_ex
+        self._timing = self._lib.cl_qgemv_native_timing
+
+    def _k_of(self, W) -> int:
+        return W.size(1)
+
+    def _validate_w(self, Wq: torch.Tensor) -> None:
+        _chk(Wq.dim() == 2, f"W_q 必须是 2 维 (N, K)，实际 {Wq.dim()} 维 (W_q must be 2-D)")
+        _chk(Wq.size(0) > 0, f"N 必须 > 0，实际 {Wq.size(0)} (N must be > 0)")
+        _chk(Wq.size(1) > 0, f"K 必须 > 0，实际 {Wq.size(1)} (K must be > 0)")
+        _chk(Wq.dtype == torch.int8,
+             f"W_q 必须是 int8（torch int8 为 kChar），实际 {Wq.dtype} (W_q must be int8)")
+        _chk(Wq.is_contiguous(), "W_q 必须是连续内存 (W_q must be contiguous)")
+        _chk(Wq.is_cuda, "W_q 必须是 CUDA 张量 (W_q must be a CUDA tensor)")
+
+    def _validate_scale(self, Wq: torch.Tensor, scale: torch.Tensor) -> None:
+        _chk(scale.dim() == 1, f"scale 必须是 1 维 (N,)，实际 {scale.dim()} 维 "
+                               "(scale must be 1-D)")
+        _chk(scale.size(0) == Wq.size(0),
+             f"scale 长度必须等于 N: scale={scale.size(0)} N={Wq.size(0)} "
+             "(len(scale) must equal N)")
+        _chk(scale.dtype == torch.float32,
+             f"scale 必须是 float32，实际 {scale.dtype} (scale must be float32)")
+        _chk(scale.is_contiguous(), "scale 必须是连续内存 (scale must be contiguous)")
+        _chk(scale.is_cuda, "scale 必须是 CUDA 张量 (scale must be a CUDA tensor)")
+        _chk(scale.device == Wq.device,
+             "scale 必须与 W_q 在同一 CUDA 设备上 (scale must be on the device of W_q)")
+
+
+_EXTS: dict = {}
+
+
+def get_ext(op: str):
+    """Singleton extension object for `op`."""
+    if op not in ("int4gemv", "qgemv"):
+        raise RuntimeError(f"unknown operator {op!r}; available: int4gemv, qgemv")
+    if op not in _EXTS:
+        _EXTS[op] = Int4gemvExt() if op == "int4gemv" else QgemvExt()
+    return _EXTS[op]

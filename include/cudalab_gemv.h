@@ -1,0 +1,120 @@
+/*
+ * cudalab_gemv.h -- C ABI of the B200 (sm_100a) weight-only quantized GEMV
+ * library libcudalab_gemv.so.
+ *
+ * Operators
+ *   INT4 (W4A16):  y[n] = sum_k (scale[n, k/128] * q[n,k]) * x[k]
+ *       W_packed uint8 [N, K/2], two 4-bit two's-complement values per byte,
+ *       low nibble = element k = 2b, high nibble = element 2b+1;
+ *       scale fp16 [N, K/128]; x fp16 [K]; y fp16 [N]; K % 128 == 0.
+ *   INT8:          y[n] = sum_k (scale[n] * W_q[n,k]) * x[k]
+ *       W_q int8 [N, K]; scale fp32 [N]; x fp16 [K]; y fp16 [N].
+ *   Both accumulate in fp32 and round once to fp16 at the end.
+ *
+ * Conventions
+ *   - All pointers are device pointers of one CUDA device (the current one),
+ *     row-major and contiguous.  Buffers are owned by the caller; no entry point
+ *     allocates device memory or synchronises the stream (except the timing
+ *     entry points, which synchronise on purpose).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every entry point returns CL_OK (0) or a CL_ERR_* status; the message of
+ *     the last failure on the calling thread is available from cl_last_error().
+ *   - A vectorised variant whose alignment contract is not met (W or x base not
+ *     16-byte aligned, or INT8 K % 16 != 0) runs the scalar baseline kernel
+ *     instead, so its output is bit-identical to the "*_baseline" variant.
+ */
+#ifndef CUDALAB_GEMV_H_
+#define CUDALAB_GEMV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define CL_OK 0
+#define CL_ERR_UNKNOWN_VARIANT 1 /* variant name not in the registry */
+#define CL_ERR_INVALID_ARGUMENT 2 /* null pointer, N/K out of contract, ... */
+#define CL_ERR_CUDA 3 /* a CUDA runtime call failed (launch, event, ...) */
+#define CL_ERR_BUFFER_TOO_SMALL 4 /* output text buffer too short */
+#define CL_ERR_DEVICE_TIMEOUT 5 /* a bounded device-side wait expired */
+
+/* ---- launch flags ---- */
+/* Launch with programmatic stream serialization: the GEMV starts streaming its
+ * weights and scales while the previous kernel in the stream finishes, and
+ * waits for that kernel before it reads x or writes y.  Only valid when W and
+ * scale are not written by the kernel immediately before it (static weights). */
+#define CL_LAUNCH_PDL 1u
+
+/* ---- variant list selectors ---- */
+#define CL_VARIANTS_NORMAL 0 /* dispatchable variants */
+#define CL_VARIANTS_ALL 1 /* including quarantined ones */
+#define CL_VARIANTS_QUARANTINED 2 /* quarantined only */
+
+/* Library version string, e.g. "cudalab-b200 0.1.0 (sm_100a)". */
+const char* cl_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* cl_last_error(void);
+
+/* Reads (and optionally clears) the bounded-wait status word of the current
+ * device: 0 = no device-side wait expired since the last clear. */
+int cl_device_status(int clear, int* status_out);
+
+/* ---- INT4 W4A16 ---- */
+
+/* Replaces the pybind entry points `forward` / `forward_into` of
+ * kernels/int4gemv/bindings.cpp:145-176 (reference interface
+ * `int4gemv_forward_into(name, Wp, scale, x, out)`); tensor-level checks
+ * (dims, dtypes, devices, contiguity) stay in the Python host wrapper, which
+ * applies them in the reference order before calling this function. */
+int cl_int4gemv(const char* variant, const uint8_t* W_packed, const void* scale, const void* x,
+                void* out, int64_t N, int64_t K, void* stream);
+
+/* Same with launch flags (CL_LAUNCH_*). */
+int cl_int4gemv_ex(const char* variant, const uint8_t* W_packed, const void* scale,
+                   const void* x, void* out, int64_t N, int64_t K, void* stream, uint32_t flags);
+
+/* Replaces `native_timing` of kernels/int4gemv/bindings.cpp:180-253: `warmup`
+ * untimed launches, then `n_windows` windows of `launches_per_window`
+ * back-to-back launches bracketed by CUDA events on `stream`; writes the
+ * per-launch microseconds of each window to per_window_us[n_windows]. */
+int cl_int4gemv_native_timing(const char* variant, const uint8_t* W_packed, const void* scale,
+                              const void* x, void* out, int64_t N, int64_t K, int64_t warmup,
+                              int64_t n_windows, int64_t launches_per_window, void* stream,
+                              uint32_t flags, double* per_window_us);
+
+/* Replaces `variants` / `all_variants` / `quarantined_variants` of
+ * kernels/int4gemv/bindings.cpp:258-285: writes the sorted names, separated by
+ * '\n' and NUL-terminated, into buf[buf_len]; *needed receives the size
+ * required including the terminator. */
+int cl_int4gemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
+
+/* ---- INT8 ---- */
+
+/* Replaces `forward` / `forward_into` of kernels/qgemv/bindings.cpp:66-115
+ * (W_q int8 [N,K], scale fp32 [N], x fp16 [K], out fp16 [N]). */
+int cl_qgemv(const char* variant, const int8_t* W_q, const float* scale, const void* x, void* out,
+             int64_t N, int64_t K, void* stream);
+
+int cl_qgemv_ex(const char* variant, const int8_t* W_q, const float* scale, const void* x,
+                void* out, int64_t N, int64_t K, void* stream, uint32_t flags);
+
+/* Replaces `native_timing` of kernels/qgemv/bindings.cpp (same contract as
+ * cl_int4gemv_native_timing). */
+int cl_qgemv_native_timing(const char* variant, const int8_t* W_q, const float* scale,
+                           const void* x, void* out, int64_t N, int64_t K, int64_t warmup,
+                           int64_t n_windows, int64_t launches_per_window, void* stream,
+                           uint32_t flags, double* per_window_us);
+
+/* Replaces `variants` / `all_variants` / `quarantined_variants` of
+ * kernels/qgemv/bindings.cpp:281-306. */
+int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* CUDALAB_GEMV_H_ */

@@ -1,0 +1,12 @@
+"""pytest configuration: registers the `gpu` marker and puts the repository
+root on sys.path.  `-m "not gpu"` runs everywhere; `-m gpu` needs a B200."""
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")

@@ -1,0 +1,115 @@
+"""Generate the golden vectors that pin the oracle and the product quantisers.
+
+Runs ONLY in the build container, where the reference tree is mounted
+(default /root/reference, override with CUDALAB_REFERENCE).  It imports the
+reference's own CPU code -- its generators (cudalab/operators/gemv.py:
+make_w/make_x), quantisers (cudalab/int4gemv_quantize.py,
+cudalab/qgemv_quantize.py), layer-A references and fp64 exact values -- and
+stores inputs and outputs as small .npz fixtures next to this script.  The
+fixtures travel; the reference does not.
+
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("CUDALAB_REFERENCE", "/root/reference"))
+
+INT4_CASES = [  # (N, K, mode, seed_w, seed_x)
+    (8, 128, "normal", 0, 1),
+    (3, 256, "mixed_sign", 0, 1),
+    (16, 512, "large", 2, 3),
+    (4, 1024, "tiny", 4, 5),
+    (2, 128, "zeros", 0, 1),
+    (32, 2048, "normal", 6, 7),
+    (5, 384, "normal", 8, 9),
+]
+INT8_CASES = [
+    (8, 64, "normal", 0, 1),
+    (16, 13, "mixed_sign", 0, 1),
+    (1, 4096, "large", 2, 3),
+    (64, 1, "normal", 4, 5),
+    (5, 7, "tiny", 6, 7),
+    (2, 16, "zeros", 0, 1),
+    (32, 1024, "normal", 8, 9),
+]
+
+
+def _bits16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def main() -> None:
+    if not REF.exists():
+        raise SystemExit(f"reference tree not found at {REF}; fixtures are committed already")
+    sys.path.insert(0, str(REF))
+    from cudalab.operators.gemv import make_w, make_x  # reference generators
+    from cudalab import int4gemv_quantize as q4
+    from cudalab import qgemv_quantize as q8
+    from cudalab.int4gemv_correctness import arith_ratio as ar4
+    from cudalab.qgemv_correctness import arith_ratio as ar8
+
+    out4 = {}
+    for i, (N, K, mode, sw, sx) in enumerate(INT4_CASES):
+        W = make_w(N, K, torch.float16, device="cpu", seed=sw, mode=mode, large=10.0)
+        if i == 6:  # one all-zero group inside an otherwise normal row
+            W.view(N, K // 128, 128)[1, 1, :] = 0
+        x = make_x(K, torch.float16, device="cpu", seed=sx, mode=mode, large=10.0)
+        Wp, s16 = q4.quantize_w(W)
+        y_ref = torch.mv(q4.dequantize_w(Wp, s16), x.float()).to(torch.float16)
+        Wq = q4.unpack_w(Wp).double()
+        a = Wq * s16.double().repeat_interleave(128, dim=1)
+        exact = torch.mv(a, x.double())
+        S = (a.abs() * x.double().abs().unsqueeze(0)).sum(dim=1)
+        ratio, _, _ = ar4(y_ref, Wp, s16, x, "float16")
+        p = f"c{i}_"
+        out4[p + "meta"] = np.array([N, K, sw, sx], np.int64)
+        out4[p + "mode"] = np.array(mode)
+        out4[p + "W_fp16"] = _bits16(W)
+        out4[p + "x"] = _bits16(x)
+        out4[p + "W_packed"] = Wp.numpy()
+        out4[p + "scale"] = _bits16(s16)
+        out4[p + "y_ref"] = _bits16(y_ref)
+        out4[p + "exact"] = exact.numpy()
+        out4[p + "S"] = S.numpy()
+        out4[p + "ref_ratio"] = np.array(ratio)
+    table = torch.arange(256, dtype=torch.uint8).view(1, 256)
+    out4["byte_table_unpacked"] = q4.unpack_w(table).numpy().astype(np.int8)
+    out4["n_cases"] = np.array(len(INT4_CASES))
+    np.savez_compressed(HERE / "int4gemv_golden.npz", **out4)
+
+    out8 = {}
+    for i, (N, K, mode, sw, sx) in enumerate(INT8_CASES):
+        W = make_w(N, K, torch.float16, device="cpu", seed=sw, mode=mode, large=10.0)
+        x = make_x(K, torch.float16, device="cpu", seed=sx, mode=mode, large=10.0)
+        Wq, s = q8.quantize_w(W)
+        y_ref = torch.mv(q8.dequantize_w(Wq, s), x.float()).to(torch.float16)
+        a = Wq.double() * s.double().unsqueeze(1)
+        exact = torch.mv(a, x.double())
+        S = (a.abs() * x.double().abs().unsqueeze(0)).sum(dim=1)
+        ratio, _, _ = ar8(y_ref, Wq, s, x, "float16")
+        p = f"c{i}_"
+        out8[p + "meta"] = np.array([N, K, sw, sx], np.int64)
+        out8[p + "mode"] = np.array(mode)
+        out8[p + "W_fp16"] = _bits16(W)
+        out8[p + "x"] = _bits16(x)
+        out8[p + "W_q"] = Wq.numpy()
+        out8[p + "scale"] = s.numpy()
+        out8[p + "y_ref"] = _bits16(y_ref)
+        out8[p + "exact"] = exact.numpy()
+        out8[p + "S"] = S.numpy()
+        out8[p + "ref_ratio"] = np.array(ratio)
+    out8["n_cases"] = np.array(len(INT8_CASES))
+    np.savez_compressed(HERE / "qgemv_golden.npz", **out8)
+    print("wrote", HERE / "int4gemv_golden.npz", HERE / "qgemv_golden.npz")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,94 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol the public
+header declares, lists variants, and rejects bad arguments with the right
+status codes before touching any device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from cudalab_b200 import _native as nat
+from cudalab_b200.build import build_library
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_library()
+    return nat.load()
+
+
+def _declared_symbols():
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"\b(cl_[a-z0-9_]+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_header_symbols_exported(lib):
+    syms = _declared_symbols()
+    assert "cl_int4gemv" in syms and "cl_qgemv" in syms
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in include/ but not exported"
+        assert s in nat.PROTOTYPES, f"{s} has no ctypes prototype"
+
+
+def test_version_and_variants(lib):
+    assert b"sm_100a" in lib.cl_version()
+    v4 = nat.list_variants("int4gemv", nat.CL_VARIANTS_NORMAL)
+    v8 = nat.list_variants("qgemv", nat.CL_VARIANTS_NORMAL)
+    assert "int4gemv_baseline" in v4 and "int4gemv_bulk" in v4 and v4 == sorted(v4)
+    assert "qgemv_baseline" in v8 and "qgemv_bulk" in v8 and v8 == sorted(v8)
+    assert nat.list_variants("int4gemv", nat.CL_VARIANTS_ALL) == v4
+    assert nat.list_variants("qgemv", nat.CL_VARIANTS_QUARANTINED) == []
+
+
+def test_list_variants_buffer_contract(lib):
+    needed = ctypes.c_size_t(0)
+    rc = lib.cl_int4gemv_list_variants(nat.CL_VARIANTS_NORMAL, None, 0, ctypes.byref(needed))
+    assert rc == nat.CL_ERR_BUFFER_TOO_SMALL and needed.value > 1
+    buf = ctypes.create_string_buffer(needed.value)
+    assert lib.cl_int4gemv_list_variants(nat.CL_VARIANTS_NORMAL, buf, needed.value,
+                                         ctypes.byref(needed)) == nat.CL_OK
+    assert lib.cl_int4gemv_list_variants(7, buf, needed.value, None) == nat.CL_ERR_INVALID_ARGUMENT
+
+
+def test_status_codes_without_device(lib):
+    # unknown variant is reported before any argument or device work
+    rc = lib.cl_int4gemv(b"no_such", None, None, None, None, 4, 128, None)
+    assert rc == nat.CL_ERR_UNKNOWN_VARIANT
+    assert "no_such" in nat.last_error(lib)
+    # N <= 0, K % 128 != 0, null pointers: rejected on the host
+    assert lib.cl_int4gemv(b"int4gemv_baseline", None, None, None, None, 0, 128, None) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert lib.cl_int4gemv(b"int4gemv_bulk", None, None, None, None, 4, 64, None) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert "128" in nat.last_error(lib)
+    assert lib.cl_int4gemv(b"int4gemv_bulk", None, None, None, None, 4, 128, None) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert lib.cl_qgemv(b"qgemv_baseline", None, None, None, None, 4, 0, None) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    buf = (ctypes.c_double * 2)()
+    assert lib.cl_qgemv_native_timing(b"qgemv_ldg", None, None, None, None, 4, 16, -1, 2, 4,
+                                      None, 0, buf) == nat.CL_ERR_INVALID_ARGUMENT
+
+
+def test_product_has_no_oracle_dependency():
+    """The package never imports the checker (oracle/)."""
+    pkg = ROOT / "cudalab_b200"
+    for f in pkg.rglob("*.py"):
+        text = f.read_text()
+        assert "import oracle" not in text and "from oracle" not in text, f
+
+
+def test_library_is_sm100a_build():
+    stamp = (ROOT / "cudalab_b200" / "_lib" / "libcudalab_gemv.stamp.json").read_text()
+    assert "compute_100a" in stamp and "sm_100a" in stamp
+
+
+def test_torch_cpu_only_here_or_gpu():
+    # documents the environment split: this file never needs a device
+    assert isinstance(torch.cuda.is_available(), bool)

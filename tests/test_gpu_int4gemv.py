@@ -1,0 +1,131 @@
+"""INT4 parity tests on the GPU (through the C ABI via the extension object).
+
+  * the 50-case layer-A suite (10 shapes x 5 modes) per variant;
+  * the 30-case negative suite per variant;
+  * the reference's golden vectors (tests/golden) on every variant;
+  * full-size BASELINE shapes against the numpy oracle's fixed bound;
+  * determinism, PDL launches, CUDA-graph capture, native timing.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from cudalab_b200 import _native as nat
+from cudalab_b200.build import build
+from cudalab_b200.int4gemv_correctness import run_suite, summarize
+from cudalab_b200.int4gemv_negative import run_negative_suite
+from cudalab_b200.operators.int4gemv import make_w4, make_x4
+from oracle import int4gemv_oracle as orc
+
+pytestmark = pytest.mark.gpu
+GOLD = np.load(Path(__file__).resolve().parent / "golden" / "int4gemv_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def ext():
+    return build("int4gemv")
+
+
+def _variants():
+    return nat.list_variants("int4gemv", nat.CL_VARIANTS_NORMAL)
+
+
+@pytest.mark.parametrize("variant", _variants())
+def test_layer_a_suite(ext, variant):
+    res = run_suite(variant, ext)
+    s = summarize(res)
+    bad = [(r.shape, r.mode, r.arith_max_ratio) for r in res if not r.passed]
+    assert s["all_pass"] and s["n_total"] == 50, bad
+    nat.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("variant", _variants())
+def test_negative_suite(ext, variant):
+    doc = run_negative_suite(ext, variant=variant)
+    bad = [(c["id"], c["status"], c["message"]) for c in doc["cases"] if not c.get("pass")]
+    assert doc["summary"]["all_pass"] and doc["summary"]["n_total"] == 30, bad
+
+
+@pytest.mark.parametrize("variant", _variants())
+def test_golden_vectors(ext, variant):
+    for i in range(int(GOLD["n_cases"])):
+        p = f"c{i}_"
+        Wp = torch.from_numpy(GOLD[p + "W_packed"]).cuda()
+        s = torch.from_numpy(GOLD[p + "scale"].view(np.float16).copy()).cuda()
+        x = torch.from_numpy(GOLD[p + "x"].view(np.float16).copy()).cuda()
+        y = ext.forward(variant, Wp, s, x).cpu().numpy()
+        K = 2 * Wp.shape[1]
+        ratio = orc.arith_ratio(y, K, GOLD[p + "exact"], GOLD[p + "S"])
+        assert np.isfinite(y.astype(np.float32)).all()
+        assert ratio <= 1.0, (i, ratio)
+
+
+FULL = [(4096, 4096), (1024, 4096), (4096, 1024), (11008, 4096), (4096, 11008)]
+
+
+@pytest.mark.parametrize("shape", FULL, ids=lambda s: f"{s[0]}x{s[1]}")
+@pytest.mark.parametrize("variant", ["int4gemv_bulk", "int4gemv_ldg", "int4gemv_bulk_f32x2"])
+def test_full_size_vs_oracle(ext, variant, shape):
+    N, K = shape
+    Wp, s, _ = make_w4(N, K, seed=77, scale=0.02)
+    x = make_x4(K, seed=78)
+    y = ext.forward(variant, Wp, s, x).cpu().numpy()
+    r = orc.check(y, Wp.cpu().numpy(), s.cpu().numpy(), x.cpu().numpy())
+    assert r["pass"], r
+
+
+@pytest.mark.parametrize("shape", [(28672, 8192), (8192, 28672)], ids=str)
+def test_sharding_shapes_row_sample(ext, shape):
+    """70B-class MLP shapes: full GEMV on the device, oracle on 512 sampled rows."""
+    N, K = shape
+    Wp, s, _ = make_w4(N, K, seed=91, scale=0.02)
+    x = make_x4(K, seed=92)
+    y = ext.forward("int4gemv_bulk", Wp, s, x).cpu().numpy()
+    rows = np.random.default_rng(0).choice(N, 512, replace=False)
+    r = orc.check(y[rows], Wp.cpu().numpy()[rows], s.cpu().numpy()[rows], x.cpu().numpy())
+    assert r["pass"], r
+
+
+@pytest.mark.parametrize("variant", _variants())
+def test_deterministic_and_pdl_identical(ext, variant):
+    Wp, s, _ = make_w4(2048, 4096, seed=5)
+    x = make_x4(4096, seed=6)
+    y0 = ext.forward(variant, Wp, s, x)
+    y1 = ext.forward(variant, Wp, s, x)
+    y2 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL)
+    assert torch.equal(y0, y1) and torch.equal(y0, y2)
+
+
+def test_graph_capture_matches_eager(ext):
+    Wps = [make_w4(1024, 2048, seed=20 + i)[:2] for i in range(4)]
+    xs = [make_x4(2048, seed=40 + i) for i in range(4)]
+    outs = [torch.empty(1024, dtype=torch.float16, device="cuda") for _ in range(4)]
+    eager = [ext.forward("int4gemv_bulk", w, s, x) for (w, s), x in zip(Wps, xs)]
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for (w, s), x, o in zip(Wps, xs, outs):
+            ext.forward_into("int4gemv_bulk", w, s, x, o, flags=nat.CL_LAUNCH_PDL)
+    st.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for (w, s), x, o in zip(Wps, xs, outs):
+            ext.forward_into("int4gemv_bulk", w, s, x, o, flags=nat.CL_LAUNCH_PDL)
+    for o in outs:
+        o.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(eager, outs):
+        assert torch.equal(a, b)
+    del g
+
+
+def test_native_timing(ext):
+    Wp, s, _ = make_w4(4096, 4096, seed=1234)
+    x = make_x4(4096, seed=1234)
+    out = torch.empty(4096, dtype=torch.float16, device="cuda")
+    d = ext.native_timing("int4gemv_bulk", Wp, s, x, out, 20, 3, 16)
+    assert set(d) >= {"variant", "median_us", "min_us", "max_us", "mean_us", "window_median_us"}
+    assert len(d["window_median_us"]) == 3 and 0 < d["min_us"] <= d["max_us"] < 1e5
+    assert nat.device_status(clear=True) == 0
