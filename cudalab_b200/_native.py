@@ -19,6 +19,7 @@ CL_ERR_BUFFER_TOO_SMALL = 4
 CL_ERR_DEVICE_TIMEOUT = 5
 
 CL_LAUNCH_PDL = 1
+CL_LAUNCH_INPUTS_READY = 2
 
 CL_VARIANTS_NORMAL = 0
 CL_VARIANTS_ALL = 1

@@ -9,7 +9,7 @@
 //   * fp32 accumulation through mixed-precision `fma.rn.f32.f16` (exact
 //     fp16 x fp16 products, one rounding per term) or packed `fma.rn.f32x2`.
 //
-// Every spin-wait is bounded by %globaltimer; on expiry the kernel records
+// Every spin-wait is bounded by the SM cycle counter; on expiry the kernel records
 // an error code in a per-translation-unit device word that the host reads
 // through the C ABI (cl_device_status) and returns without touching more
 // memory.
@@ -32,7 +32,10 @@ constexpr int kMaxSliceBytes = kConsumerThreads * kChunkBytes;               // 
 constexpr int kRingBytes = 64 * 1024;               // weight staging ring per CTA
 constexpr int kMaxStages = 16;
 constexpr int kScaleSmemBytes = 32 * 1024;          // per-CTA cache of group scales
-constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
+// Bound of every spin-wait, in SM clock cycles (~2 s at 2 GHz).  The SM-local
+// cycle counter is used because reading %globaltimer is a slow,
+// long-latency operation that would dominate a short wait.
+constexpr long long kWaitTimeoutCycles = 4000000000ll;
 
 // Error codes written to the device status word.
 constexpr int kStatusOk = 0;
@@ -46,12 +49,6 @@ constexpr int kStatusTimeoutDrain = 4;   // producer gave up draining its copies
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long global_timer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -91,15 +88,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait on one mbarrier phase. Returns false when the budget expired.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_timer_ns();
-#pragma unroll 1
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitTimeoutCycles) return false;
     }
+    return true;
 }
 
 // One bulk (TMA engine) copy global -> shared, completing on `bar`.
@@ -162,6 +157,21 @@ __device__ __forceinline__ uint32_t lop3_sel_xor(uint32_t a, uint32_t b, uint32_
     return d;
 }
 
+// Same with the mask and the exponent pattern as instruction immediates.
+template <uint32_t B, uint32_t C>
+__device__ __forceinline__ uint32_t lop3_sel_xor_i(uint32_t a) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "n"(B), "n"(C));
+    return d;
+}
+
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt_i(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "n"(SEL));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
@@ -193,10 +203,10 @@ __device__ __forceinline__ void int4x8_to_h2(uint32_t w, __half2 (&q)[4]) {
     const uint32_t hi = w >> 8;
     const __half2 one = h2_const(kH_one), sixteenth = h2_const(kH_1_16);
     const __half2 b0 = h2_const(kH_m1032), b1 = h2_const(kH_m72);
-    q[0] = __hfma2(u32_as_h2(lop3_sel_xor(w, 0x000F000Fu, 0x64086408u)), one, b0);
-    q[1] = __hfma2(u32_as_h2(lop3_sel_xor(w, 0x00F000F0u, 0x64806480u)), sixteenth, b1);
-    q[2] = __hfma2(u32_as_h2(lop3_sel_xor(hi, 0x000F000Fu, 0x64086408u)), one, b0);
-    q[3] = __hfma2(u32_as_h2(lop3_sel_xor(hi, 0x00F000F0u, 0x64806480u)), sixteenth, b1);
+    q[0] = __hfma2(u32_as_h2(lop3_sel_xor_i<0x000F000Fu, 0x64086408u>(w)), one, b0);
+    q[1] = __hfma2(u32_as_h2(lop3_sel_xor_i<0x00F000F0u, 0x64806480u>(w)), sixteenth, b1);
+    q[2] = __hfma2(u32_as_h2(lop3_sel_xor_i<0x000F000Fu, 0x64086408u>(hi)), one, b0);
+    q[3] = __hfma2(u32_as_h2(lop3_sel_xor_i<0x00F000F0u, 0x64806480u>(hi)), sixteenth, b1);
 }
 
 // 4 signed bytes -> 2 half2 of exact integers: (b0,b1) (b2,b3).
@@ -205,8 +215,8 @@ __device__ __forceinline__ void int4x8_to_h2(uint32_t w, __half2 (&q)[4]) {
 __device__ __forceinline__ void int8x4_to_h2(uint32_t w, __half2 (&q)[2]) {
     const uint32_t u = w ^ 0x80808080u;
     const __half2 one = h2_const(kH_one), b = h2_const(kH_m1152);
-    q[0] = __hfma2(u32_as_h2(prmt(u, 0x64646464u, 0x5140u)), one, b);
-    q[1] = __hfma2(u32_as_h2(prmt(u, 0x64646464u, 0x7362u)), one, b);
+    q[0] = __hfma2(u32_as_h2(prmt_i<0x5140u>(u, 0x64646464u)), one, b);
+    q[1] = __hfma2(u32_as_h2(prmt_i<0x7362u>(u, 0x64646464u)), one, b);
 }
 
 // d = a * b + c with a, b binary16 and c, d binary32: the product is exact in

@@ -21,6 +21,7 @@
 
 #include "gemv_launch.h"
 #include "gemv_vector.cuh"
+#include "gemv_mma.cuh"
 
 namespace clb {
 
@@ -111,7 +112,7 @@ cudaError_t ensure_smem_attr(K kernel, int dev, int bytes, int slot) {
     std::lock_guard<std::mutex> lock(mu);
     if (done[slot][dev] >= bytes) return cudaSuccess;
     // always request the largest size this kernel can ever use
-    const int want = std::max(bytes, kSmemCap);
+    const int want = bytes > kSmemCap ? bytes : kSmemCap;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
     if (e == cudaSuccess) done[slot][dev] = want;
     return e;
@@ -219,12 +220,66 @@ cudaError_t launch_vec(const void* W, const void* scale, const void* x, void* y,
                   static_cast<__half*>(y), g);
 }
 
+// Geometry of the tensor-core kernels (see gemv_mma.cuh).  Returns false when
+// the staged activations do not fit in shared memory (K beyond ~100k).
+bool make_mma_geom(int64_t N, int64_t K, bool int4, int num_sms, MmaGeom& g) {
+    g = MmaGeom{};
+    g.N = N;
+    g.K = K;
+    g.row_bytes = int4 ? K / 2 : K;
+    g.blocks = (int32_t)(g.row_bytes / 64);
+    g.n_kc = (g.blocks + kMmaChunkBlocks - 1) / kMmaChunkBlocks;
+    int64_t ctas = std::min<int64_t>(N, num_sms);
+    for (;;) {
+        const int64_t rows = (N + ctas - 1) / ctas;
+        if (((rows + 15) / 16) * g.n_kc <= kMmaPartialMax || ctas >= N) break;
+        ctas = std::min<int64_t>(N, ctas + std::max<int64_t>(1, ctas / 8));
+    }
+    g.ctas = (int32_t)ctas;
+    g.rows_base = (int32_t)(N / ctas);
+    g.rows_rem = (int32_t)(N % ctas);
+    g.max_rows = g.rows_base + (g.rows_rem > 0 ? 1 : 0);
+    g.max_items = (int32_t)(((g.max_rows + 15) / 16) * g.n_kc);
+    if (g.max_items > kMmaPartialMax) return false;
+    g.xs_bytes = (int32_t)(K * 2);
+    return mma_smem_total(g) <= 227 * 1024;
+}
+
+template <class Fmt, int kWarps, int kSlot>
+cudaError_t launch_mma(const void* W, const void* scale, const void* x, void* y, int64_t N,
+                       int64_t K, cudaStream_t s, unsigned flags) {
+    constexpr bool kInt4 = Fmt::kGroupScale;
+    const bool ok = aligned16(W) && aligned16(x) && (kInt4 ? (K % 128 == 0) : (K % 64 == 0));
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    MmaGeom g;
+    if (!ok || !make_mma_geom(N, K, kInt4, sm_count(dev), g)) {
+        return kInt4 ? launch_int4_scalar(W, scale, x, y, N, K, s, flags)
+                     : launch_int8_scalar(W, scale, x, y, N, K, s, flags);
+    }
+    g.early_x = (flags & 3u) == 3u ? 1 : 0;
+    const int smem = mma_smem_total(g);
+    const bool all_full = (g.blocks % kMmaChunkBlocks) == 0;
+    auto kernel = all_full ? gemv_mma_kernel<Fmt, kWarps, true> : gemv_mma_kernel<Fmt, kWarps, false>;
+    if (smem > 48 * 1024) {
+        e = ensure_smem_attr(kernel, dev, 227 * 1024, kSlot + (all_full ? 0 : 4));
+        if (e != cudaSuccess) return e;
+    }
+    using S = typename Fmt::Scale;
+    return launch(kernel, dim3((unsigned)g.ctas), dim3(32 * kWarps), (size_t)smem, s,
+                  flags, static_cast<const uint8_t*>(W), static_cast<const S*>(scale),
+                  static_cast<const __half*>(x), static_cast<__half*>(y), g);
+}
+
 const VariantDesc kInt4Variants[] = {
     {"int4gemv_baseline", launch_int4_scalar, false},
     {"int4gemv_bulk", launch_vec<Int4Fmt, MathF16, true, 0>, false},
     {"int4gemv_bulk_f32x2", launch_vec<Int4Fmt, MathF32x2, true, 1>, false},
     {"int4gemv_ldg", launch_vec<Int4Fmt, MathF16, false, 2>, false},
     {"int4gemv_ldg_f32x2", launch_vec<Int4Fmt, MathF32x2, false, 3>, false},
+    {"int4gemv_mma", launch_mma<MmaInt4, 8, 8>, false},
+    {"int4gemv_mma16", launch_mma<MmaInt4, 16, 10>, false},
 };
 
 const VariantDesc kInt8Variants[] = {
@@ -233,6 +288,8 @@ const VariantDesc kInt8Variants[] = {
     {"qgemv_bulk_f32x2", launch_vec<Int8Fmt, MathF32x2, true, 5>, false},
     {"qgemv_ldg", launch_vec<Int8Fmt, MathF16, false, 6>, false},
     {"qgemv_ldg_f32x2", launch_vec<Int8Fmt, MathF32x2, false, 7>, false},
+    {"qgemv_mma", launch_mma<MmaInt8, 8, 9>, false},
+    {"qgemv_mma16", launch_mma<MmaInt8, 16, 11>, false},
 };
 
 }  // namespace
@@ -248,15 +305,17 @@ const VariantDesc* int8_variants(int* count) {
 }
 
 cudaError_t read_device_status(int clear, int* status) {
-    int v = 0;
+    int v = 0, m = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_vec_status, sizeof(int));
+
     if (e != cudaSuccess) return e;
     if (clear) {
         const int zero = 0;
         e = cudaMemcpyToSymbol(g_vec_status, &zero, sizeof(int));
+
         if (e != cudaSuccess) return e;
     }
-    *status = v;
+    *status = v ? v : m;
     return cudaSuccess;
 }
 

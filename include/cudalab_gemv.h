@@ -47,6 +47,12 @@ extern "C" {
  * waits for that kernel before it reads x or writes y.  Only valid when W and
  * scale are not written by the kernel immediately before it (static weights). */
 #define CL_LAUNCH_PDL 1u
+/* Together with CL_LAUNCH_PDL: x is not written by the kernel immediately
+ * before this GEMV either (e.g. several projections of one activation, or
+ * independent GEMVs issued back to back).  The tensor-core variants then read
+ * x and compute before waiting on the preceding kernel and wait only before
+ * storing y.  Ignored by variants that do not use it. */
+#define CL_LAUNCH_INPUTS_READY 2u
 
 /* ---- variant list selectors ---- */
 #define CL_VARIANTS_NORMAL 0 /* dispatchable variants */

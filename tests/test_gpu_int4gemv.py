@@ -66,7 +66,7 @@ FULL = [(4096, 4096), (1024, 4096), (4096, 1024), (11008, 4096), (4096, 11008)]
 
 
 @pytest.mark.parametrize("shape", FULL, ids=lambda s: f"{s[0]}x{s[1]}")
-@pytest.mark.parametrize("variant", ["int4gemv_bulk", "int4gemv_ldg", "int4gemv_bulk_f32x2"])
+@pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_bulk", "int4gemv_ldg"])
 def test_full_size_vs_oracle(ext, variant, shape):
     N, K = shape
     Wp, s, _ = make_w4(N, K, seed=77, scale=0.02)
@@ -82,7 +82,7 @@ def test_sharding_shapes_row_sample(ext, shape):
     N, K = shape
     Wp, s, _ = make_w4(N, K, seed=91, scale=0.02)
     x = make_x4(K, seed=92)
-    y = ext.forward("int4gemv_bulk", Wp, s, x).cpu().numpy()
+    y = ext.forward("int4gemv_mma", Wp, s, x).cpu().numpy()
     rows = np.random.default_rng(0).choice(N, 512, replace=False)
     r = orc.check(y[rows], Wp.cpu().numpy()[rows], s.cpu().numpy()[rows], x.cpu().numpy())
     assert r["pass"], r
@@ -95,7 +95,8 @@ def test_deterministic_and_pdl_identical(ext, variant):
     y0 = ext.forward(variant, Wp, s, x)
     y1 = ext.forward(variant, Wp, s, x)
     y2 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL)
-    assert torch.equal(y0, y1) and torch.equal(y0, y2)
+    y3 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY)
+    assert torch.equal(y0, y1) and torch.equal(y0, y2) and torch.equal(y0, y3)
 
 
 def test_graph_capture_matches_eager(ext):

@@ -56,7 +56,7 @@ def test_golden_vectors(ext, variant):
 
 @pytest.mark.parametrize("shape", [(4096, 4096), (11008, 4096), (4096, 11008), (4096, 1024)],
                          ids=lambda s: f"{s[0]}x{s[1]}")
-@pytest.mark.parametrize("variant", ["qgemv_bulk", "qgemv_ldg", "qgemv_bulk_f32x2"])
+@pytest.mark.parametrize("variant", ["qgemv_mma", "qgemv_bulk", "qgemv_ldg"])
 def test_full_size_vs_oracle(ext, variant, shape):
     N, K = shape
     Wq, s, _ = make_w_q(N, K, seed=17, scale=0.02)
@@ -73,5 +73,6 @@ def test_deterministic_and_pdl_identical(ext, variant):
     y0 = ext.forward(variant, Wq, s, x)
     y1 = ext.forward(variant, Wq, s, x)
     y2 = ext.forward(variant, Wq, s, x, flags=nat.CL_LAUNCH_PDL)
-    assert torch.equal(y0, y1) and torch.equal(y0, y2)
+    y3 = ext.forward(variant, Wq, s, x, flags=nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY)
+    assert torch.equal(y0, y1) and torch.equal(y0, y2) and torch.equal(y0, y3)
     assert nat.device_status(clear=True) == 0
