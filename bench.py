@@ -6,8 +6,13 @@ Workload (BASELINE metric "W4A16 GEMV us & HBM GB/s at 4096x4096, streaming"):
   a pool of 64 independently seeded weight sets (64 x 8.67 MB = 555 MB, far
   above the 126 MB L2) and 64 x / y buffers, cycled launch by launch, so every
   launch streams its weights from HBM.  One step = one pass over the pool (64
-  GEMVs), captured once in a CUDA graph with programmatic dependent launch
-  between consecutive GEMVs and replayed.
+  GEMVs), captured once in a CUDA graph and replayed.  Consecutive GEMVs use
+  programmatic dependent launch; in the streaming regime the activations of a
+  GEMV are not produced by the GEMV before it (CL_LAUNCH_INPUTS_READY), so a
+  GEMV streams its weights and computes while the previous one finishes and
+  only its store of y waits.  The same pool is also timed as a fully
+  dependent chain (CL_LAUNCH_PDL: x read after the previous kernel completes)
+  and with plain stream order, and the INT8 sibling on the same harness.
 
 value   = algorithmic bytes moved by all ranks / max-over-ranks device time
           (GB/s; bytes per GEMV = N*K/2 + N*K/64 + 2K + 2N = 8,667,136).
@@ -204,13 +209,16 @@ def cpu_baseline_sample():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--variant", default="int4gemv_bulk")
-    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--variant", default="int4gemv_mma")
+    ap.add_argument("--int8-variant", default="qgemv_mma")
+    ap.add_argument("--mode", default="streaming", choices=["streaming", "dependent", "serial"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--context-reps", type=int, default=200,
+                    help="graph replays for the other-mode and INT8 context timings")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -233,19 +241,41 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     ext = build("int4gemv")
-    flags = 0 if args.no_pdl else nat.CL_LAUNCH_PDL
+    mode_flags = {"streaming": nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY,
+                  "dependent": nat.CL_LAUNCH_PDL, "serial": 0}
+    flags = mode_flags[args.mode]
     pool = op.make_bench_pool(N_ROWS, K_COLS, mode="l2cold", pool_size=POOL, weight_dist=0.02)
 
     # ---- capture one pass over the pool ----
     s = torch.cuda.Stream()
-    with torch.cuda.stream(s):
-        for i in range(POOL):
-            pool.launch(ext, args.variant, i, flags=flags)
-    s.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
-        for i in range(POOL):
-            pool.launch(ext, args.variant, i, flags=flags)
+
+    def capture(p, e, variant, fl):
+        with torch.cuda.stream(s):
+            for i in range(POOL):
+                p.launch(e, variant, i, flags=fl)
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(POOL):
+                p.launch(e, variant, i, flags=fl)
+        return graph
+
+    def replay_us(graph, reps):
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                graph.replay()
+        s.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            a.record(s)
+            for _ in range(reps):
+                graph.replay()
+            b.record(s)
+        b.synchronize()
+        return a.elapsed_time(b) * 1e3 / (reps * POOL)
+
+    g = capture(pool, ext, args.variant, flags)
 
     def barrier():
         if world > 1:
@@ -264,12 +294,14 @@ def main():
     e1 = torch.cuda.Event(enable_timing=True)
     barrier()
     sampler.mark("t0")
+    torch.cuda.nvtx.range_push("timed")
     with torch.cuda.stream(s):
         e0.record(s)
         for _ in range(args.steps):
             g.replay()
         e1.record(s)
     barrier()
+    torch.cuda.nvtx.range_pop()
     sampler.mark("t1")
     ms = e0.elapsed_time(e1)
     time.sleep(0.25)
@@ -314,6 +346,21 @@ def main():
         e2e_s = float(t.item())
     e2e_val = bytes_per * POOL * args.e2e_steps * world / e2e_s / 1e9
 
+    # ---- context on the same box: other dependency modes and the INT8 sibling ----
+    modes_us = {args.mode: round(us_per_gemv, 4)}
+    for m, fl in mode_flags.items():
+        if m != args.mode:
+            gm = capture(pool, ext, args.variant, fl)
+            modes_us[m] = round(replay_us(gm, args.context_reps), 4)
+            del gm
+    from cudalab_b200.operators.qgemv import qgemv as op8, algorithmic_bytes_int8
+    ext8 = build("qgemv")
+    pool8 = op8.make_bench_pool(N_ROWS, K_COLS, mode="l2cold", pool_size=POOL, weight_dist=0.02)
+    g8 = capture(pool8, ext8, args.int8_variant, flags)
+    us8 = replay_us(g8, args.context_reps)
+    del g8, pool8
+    status = status or nat.device_status(clear=True)
+
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -331,7 +378,7 @@ def main():
             "data": "synthetic: seeded W ~ N(0,0.02^2) quantised G=128, x ~ N(0,1)",
             "config": {"workload": "int4gemv W4A16 4096x4096 G=128, L2-cold pool of 64 weight "
                                    "sets (555 MB, inputs larger than L2), 64 GEMVs per step, "
-                                   "CUDA graph" + ("" if args.no_pdl else " + PDL"),
+                                   "CUDA graph, " + args.mode + " mode",
                        "N": N_ROWS, "K": K_COLS, "pool": POOL, "variant": args.variant,
                        "l2": "inputs larger than L2 (pool cycled)",
                        "parallelism": f"replicas x{world}"},
@@ -349,6 +396,10 @@ def main():
                     "us_per_gemv": round(e2e_s * 1e6 / (POOL * args.e2e_steps), 2),
                     "note": "public API (forward_into over the C ABI) per GEMV: pinned x H2D, "
                             "launch, y D2H; wall clock; weights resident"},
+            "modes_us_per_gemv": modes_us,
+            "int8": {"variant": args.int8_variant, "us_per_gemv": round(us8, 4),
+                     "gbs": round(algorithmic_bytes_int8(N_ROWS, K_COLS) / (us8 * 1e-6) / 1e9, 1),
+                     "int4_over_int8_speedup": round(us8 / us_per_gemv, 3)},
             "gpu_launches": launches,
             "device_status": status,
             "clocks": sampler.summary(),
