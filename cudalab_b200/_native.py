@@ -51,7 +51,19 @@ PROTOTYPES = {
     "cl_qgemv_native_timing": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                       _vp, _u32, _dp]),
     "cl_qgemv_list_variants": (_int, [_int, ctypes.c_char_p, _size, ctypes.POINTER(_size)]),
+    "cl_peer_alloc": (_int, [_size, ctypes.POINTER(_vp), _vp]),
+    "cl_peer_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "cl_peer_close": (_int, [_vp]),
+    "cl_peer_free": (_int, [_vp]),
+    "cl_int4gemv_sharded": (_int, [_cs, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64,
+                                   _i64, _vp, _u32]),
+    "cl_qgemv_sharded": (_int, [_cs, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64,
+                                _i64, _vp, _u32]),
 }
+
+CL_MAX_PEERS = 8
+CL_IPC_HANDLE_BYTES = 64
+CL_PEER_FLAG_BYTES = 64
 
 
 def load(path: Path | None = None) -> ctypes.CDLL:

@@ -143,6 +143,61 @@ int timing(const clb::VariantDesc* table, int n, const char* op, const char* var
     return rc;
 }
 
+const clb::ShardedVariantDesc* find_sharded(const clb::ShardedVariantDesc* t, int n,
+                                             const char* name) {
+    if (name == nullptr) return nullptr;
+    for (int i = 0; i < n; ++i)
+        if (std::strcmp(t[i].name, name) == 0) return &t[i];
+    return nullptr;
+}
+
+int run_sharded(const clb::ShardedVariantDesc* table, int n, const char* op, const char* variant,
+                const void* W, const void* scale, const void* x, void* const* y_peers,
+                void* const* flag_peers, int rank, int world, int64_t row0, int64_t N_shard,
+                int64_t N_total, int64_t K, void* stream, uint32_t flags, bool is_int4) {
+    const std::string o(op);
+    const clb::ShardedVariantDesc* v = find_sharded(table, n, variant);
+    if (!v) {
+        std::string m = "unknown " + o + " sharded variant '" + (variant ? variant : "(null)") +
+                        "'; available: ";
+        for (int i = 0; i < n; ++i) m += std::string(table[i].name) + " ";
+        return fail(CL_ERR_UNKNOWN_VARIANT, m);
+    }
+    int rc = check_args(op, W, scale, x, y_peers, N_shard, K, is_int4);
+    if (rc != CL_OK) return rc;
+    if (world < 1 || world > CL_MAX_PEERS)
+        return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: world must be in [1, 8]");
+    if (rank < 0 || rank >= world)
+        return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: rank out of range");
+    if (row0 < 0 || N_total <= 0 || row0 + N_shard > N_total)
+        return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: shard rows outside [0, N_total)");
+    if (!is_int4 && (K % 64) != 0)
+        return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: K must be divisible by 64");
+    if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(x)) & 15u)
+        return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: W and x must be 16-byte aligned");
+    if (!flag_peers) return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: null flag pointers");
+    clb::PeerArgs pa{};
+    for (int p = 0; p < world; ++p) {
+        if (!y_peers[p] || !y_peers[world + p] || !flag_peers[p])
+            return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: null peer pointer");
+        pa.y[0][p] = y_peers[p];
+        pa.y[1][p] = y_peers[world + p];
+        pa.flag[p] = static_cast<unsigned*>(flag_peers[p]);
+    }
+    pa.row0 = row0;
+    pa.rank = rank;
+    pa.world = world;
+    cudaError_t e = v->fn(W, scale, x, pa, N_shard, K, static_cast<cudaStream_t>(stream), flags);
+    if (e != cudaSuccess) {
+        char ctx[160];
+        std::snprintf(ctx, sizeof ctx, "sharded kernel launch (rank %d/%d, rows %lld+%lld of %lld, K %lld)",
+                      rank, world, (long long)row0, (long long)N_shard, (long long)N_total,
+                      (long long)K);
+        return cuda_fail(e, ctx);
+    }
+    return CL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -214,6 +269,71 @@ int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed)
     int n = 0;
     const clb::VariantDesc* t = clb::int8_variants(&n);
     return list_variants(t, n, which, buf, buf_len, needed);
+}
+
+// ---- peer buffers and the row-sharded GEMV ----
+int cl_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+    if (!ptr || !ipc_handle || bytes == 0)
+        return fail(CL_ERR_INVALID_ARGUMENT, "peer_alloc: null output or zero size");
+    static_assert(sizeof(cudaIpcMemHandle_t) == CL_IPC_HANDLE_BYTES, "IPC handle size");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "peer_alloc: cudaMalloc");
+    if ((e = cudaMemset(p, 0, bytes)) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "peer_alloc: cudaMemset");
+    }
+    cudaIpcMemHandle_t h;
+    if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "peer_alloc: cudaIpcGetMemHandle");
+    }
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *ptr = p;
+    return CL_OK;
+}
+
+int cl_peer_open(const void* ipc_handle, void** peer_ptr) {
+    if (!ipc_handle || !peer_ptr) return fail(CL_ERR_INVALID_ARGUMENT, "peer_open: null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "peer_open: cudaIpcOpenMemHandle");
+    return CL_OK;
+}
+
+int cl_peer_close(void* peer_ptr) {
+    if (!peer_ptr) return fail(CL_ERR_INVALID_ARGUMENT, "peer_close: null pointer");
+    cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+    if (e != cudaSuccess) return cuda_fail(e, "peer_close: cudaIpcCloseMemHandle");
+    return CL_OK;
+}
+
+int cl_peer_free(void* ptr) {
+    if (!ptr) return fail(CL_ERR_INVALID_ARGUMENT, "peer_free: null pointer");
+    cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) return cuda_fail(e, "peer_free: cudaFree");
+    return CL_OK;
+}
+
+int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void* scale_shard,
+                        const void* x, void* const* y_peers, void* const* flag_peers, int rank,
+                        int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
+                        void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::ShardedVariantDesc* t = clb::int4_sharded_variants(&n);
+    return run_sharded(t, n, "int4gemv", variant, W_shard, scale_shard, x, y_peers, flag_peers,
+                       rank, world, row0, N_shard, N_total, K, stream, flags, true);
+}
+
+int cl_qgemv_sharded(const char* variant, const int8_t* W_shard, const float* scale_shard,
+                     const void* x, void* const* y_peers, void* const* flag_peers, int rank,
+                     int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
+                     void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::ShardedVariantDesc* t = clb::int8_sharded_variants(&n);
+    return run_sharded(t, n, "qgemv", variant, W_shard, scale_shard, x, y_peers, flag_peers,
+                       rank, world, row0, N_shard, N_total, K, stream, flags, false);
 }
 
 }  // extern "C"

@@ -43,6 +43,14 @@ constexpr int kStatusTimeoutFull = 1;    // consumer gave up waiting for a tile
 constexpr int kStatusTimeoutEmpty = 2;   // producer gave up waiting for a slot
 constexpr int kStatusTimeoutScale = 3;   // consumer gave up waiting for scales
 constexpr int kStatusTimeoutDrain = 4;   // producer gave up draining its copies
+constexpr int kStatusTimeoutPeer = 5;    // a sharded GEMV gave up waiting for a peer rank
+
+// Per-device status word for bounded waits (one per translation unit that
+// includes this header; read through the C ABI).  The first code recorded
+// since the last clear wins.
+static __device__ int g_status;
+
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_status, 0, code); }
 
 // ---------------------------------------------------------------------------
 // Small PTX wrappers.
@@ -116,6 +124,17 @@ __device__ __forceinline__ void pdl_wait_prior_grids() {
 }
 __device__ __forceinline__ void pdl_allow_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// System-scope release store / acquire load of a flag word that other GPUs
+// read or write through peer mappings.
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // Named barrier among the consumer warps only (the producer warp never joins).

@@ -17,7 +17,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "gemv_launch.h"
 #include "gemv_vector.cuh"
@@ -84,10 +86,6 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 
-// Largest dynamic shared memory any vectorised kernel can request.
-constexpr int kSmemCap =
-    kRingBytes + kScaleSmemBytes + 2 * kConsumerWarps * 4 * 4 + 2 * kMaxStages * 8 + 64;
-
 int sm_count(int dev) {
     static int cache[kMaxDevices] = {0};
     if (dev < 0 || dev >= kMaxDevices) return 148;
@@ -103,18 +101,25 @@ int sm_count(int dev) {
 // Opt a kernel into more than 48 KiB of dynamic shared memory, once per
 // device and kernel.
 template <class K>
-cudaError_t ensure_smem_attr(K kernel, int dev, int bytes, int slot) {
+cudaError_t ensure_smem_attr(K kernel, int dev, int bytes) {
     static std::mutex mu;
-    static int done[16][kMaxDevices] = {{0}};
+    static std::map<std::pair<const void*, int>, int> done;
     if (bytes <= 48 * 1024) return cudaSuccess;
-    if (dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= 16)
-        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     std::lock_guard<std::mutex> lock(mu);
-    if (done[slot][dev] >= bytes) return cudaSuccess;
-    // always request the largest size this kernel can ever use
-    const int want = bytes > kSmemCap ? bytes : kSmemCap;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
-    if (e == cudaSuccess) done[slot][dev] = want;
+    const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    // request the largest dynamic size this kernel can ever use: the opt-in
+    // limit of the device minus the kernel's static shared memory
+    int optin = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa{};
+    if ((e = cudaFuncGetAttributes(&fa, kernel)) != cudaSuccess) return e;
+    const int want = optin - (int)fa.sharedSizeBytes;
+    if (want < bytes) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e == cudaSuccess) done[key] = want;
     return e;
 }
 
@@ -193,7 +198,7 @@ cudaError_t launch_int8_scalar(const void* W, const void* scale, const void* x, 
                   static_cast<const __half*>(x), static_cast<__half*>(y), N, K);
 }
 
-template <class Fmt, class Math, bool kBulk, int kSlot>
+template <class Fmt, class Math, bool kBulk>
 cudaError_t launch_vec(const void* W, const void* scale, const void* x, void* y, int64_t N,
                        int64_t K, cudaStream_t s, unsigned flags) {
     constexpr bool kInt4 = Fmt::kGroupScale;
@@ -210,7 +215,7 @@ cudaError_t launch_vec(const void* W, const void* scale, const void* x, void* y,
     const GemvGeom g = make_geom(N, K, kInt4, kBulk, sm_count(dev));
     const int smem = smem_total(g);
     auto kernel = gemv_vec_kernel<Fmt, Math, kBulk>;
-    e = ensure_smem_attr(kernel, dev, smem, kSlot);
+    e = ensure_smem_attr(kernel, dev, smem);
     if (e != cudaSuccess) return e;
     const dim3 grid((unsigned)g.ctas);
     const dim3 block(kBulk ? kConsumerThreads + 32 : kConsumerThreads);
@@ -222,77 +227,160 @@ cudaError_t launch_vec(const void* W, const void* scale, const void* x, void* y,
 
 // Geometry of the tensor-core kernels (see gemv_mma.cuh).  Returns false when
 // the staged activations do not fit in shared memory (K beyond ~100k).
-bool make_mma_geom(int64_t N, int64_t K, bool int4, int num_sms, MmaGeom& g) {
+// ctas_per_sm: CTAs of one GEMV per SM before tiles are shared (1 for 8-warp
+// CTAs; 2 for 4-warp CTAs keeps the warps of one GEMV per SM unchanged).
+bool make_mma_geom(int64_t N, int64_t K, bool int4, int num_sms, int ctas_per_sm, MmaGeom& g) {
     g = MmaGeom{};
     g.N = N;
     g.K = K;
     g.row_bytes = int4 ? K / 2 : K;
     g.blocks = (int32_t)(g.row_bytes / 64);
     g.n_kc = (g.blocks + kMmaChunkBlocks - 1) / kMmaChunkBlocks;
-    int64_t ctas = std::min<int64_t>(N, num_sms);
+    const int64_t tiles = (N + 15) / 16;
+    int64_t ctas = std::min<int64_t>(tiles, (int64_t)num_sms * ctas_per_sm);
     for (;;) {
-        const int64_t rows = (N + ctas - 1) / ctas;
-        if (((rows + 15) / 16) * g.n_kc <= kMmaPartialMax || ctas >= N) break;
-        ctas = std::min<int64_t>(N, ctas + std::max<int64_t>(1, ctas / 8));
+        const int64_t per = (tiles + ctas - 1) / ctas;
+        if (per * g.n_kc <= kMmaPartialMax || ctas >= tiles) break;
+        ctas = std::min<int64_t>(tiles, ctas + std::max<int64_t>(1, ctas / 8));
     }
     g.ctas = (int32_t)ctas;
-    g.rows_base = (int32_t)(N / ctas);
-    g.rows_rem = (int32_t)(N % ctas);
-    g.max_rows = g.rows_base + (g.rows_rem > 0 ? 1 : 0);
-    g.max_items = (int32_t)(((g.max_rows + 15) / 16) * g.n_kc);
+    g.tiles_base = (int32_t)(tiles / ctas);
+    g.tiles_rem = (int32_t)(tiles % ctas);
+    const int64_t max_tiles = g.tiles_base + (g.tiles_rem > 0 ? 1 : 0);
+    g.max_rows = (int32_t)std::min<int64_t>(16 * max_tiles, N);
+    g.max_items = (int32_t)(max_tiles * g.n_kc);
     if (g.max_items > kMmaPartialMax) return false;
     g.xs_bytes = (int32_t)(K * 2);
-    return mma_smem_total(g) <= 227 * 1024;
+    return mma_smem_total(g) <= 226 * 1024;  // 1 KiB left for static shared memory
 }
 
-template <class Fmt, int kWarps, int kSlot>
-cudaError_t launch_mma(const void* W, const void* scale, const void* x, void* y, int64_t N,
-                       int64_t K, cudaStream_t s, unsigned flags) {
+template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer>
+cudaError_t launch_mma_impl(const void* W, const void* scale, const void* x, void* y, int64_t N,
+                            int64_t K, cudaStream_t s, unsigned flags, const PeerOut& po) {
     constexpr bool kInt4 = Fmt::kGroupScale;
     const bool ok = aligned16(W) && aligned16(x) && (kInt4 ? (K % 128 == 0) : (K % 64 == 0));
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     MmaGeom g;
-    if (!ok || !make_mma_geom(N, K, kInt4, sm_count(dev), g)) {
+    if constexpr (kPeer) {
+        // the sharded entry points check this contract before launching
+        if (!ok) return cudaErrorMisalignedAddress;
+        if (!make_mma_geom(N, K, kInt4, sm_count(dev), kCtasPerSm, g))
+            return cudaErrorInvalidConfiguration;
+    } else if (!ok || !make_mma_geom(N, K, kInt4, sm_count(dev), kCtasPerSm, g)) {
         return kInt4 ? launch_int4_scalar(W, scale, x, y, N, K, s, flags)
                      : launch_int8_scalar(W, scale, x, y, N, K, s, flags);
     }
     g.early_x = (flags & 3u) == 3u ? 1 : 0;
     const int smem = mma_smem_total(g);
     const bool all_full = (g.blocks % kMmaChunkBlocks) == 0;
-    auto kernel = all_full ? gemv_mma_kernel<Fmt, kWarps, true> : gemv_mma_kernel<Fmt, kWarps, false>;
+    auto kernel = all_full ? gemv_mma_kernel<Fmt, kWarps, true, kPeer>
+                           : gemv_mma_kernel<Fmt, kWarps, false, kPeer>;
     if (smem > 48 * 1024) {
-        e = ensure_smem_attr(kernel, dev, 227 * 1024, kSlot + (all_full ? 0 : 4));
+        e = ensure_smem_attr(kernel, dev, smem);
         if (e != cudaSuccess) return e;
     }
     using S = typename Fmt::Scale;
-    return launch(kernel, dim3((unsigned)g.ctas), dim3(32 * kWarps), (size_t)smem, s,
-                  flags, static_cast<const uint8_t*>(W), static_cast<const S*>(scale),
-                  static_cast<const __half*>(x), static_cast<__half*>(y), g);
+    return launch(kernel, dim3((unsigned)g.ctas), dim3(32 * kWarps), (size_t)smem, s, flags,
+                  static_cast<const uint8_t*>(W), static_cast<const S*>(scale),
+                  static_cast<const __half*>(x), static_cast<__half*>(y), g, po);
+}
+
+template <class Fmt, int kWarps, int kCtasPerSm>
+cudaError_t launch_mma(const void* W, const void* scale, const void* x, void* y, int64_t N,
+                       int64_t K, cudaStream_t s, unsigned flags) {
+    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, false>(W, scale, x, y, N, K, s, flags,
+                                                           PeerOut{});
+}
+
+template <class Fmt, int kWarps, int kCtasPerSm>
+cudaError_t launch_mma_sharded(const void* W, const void* scale, const void* x,
+                               const PeerArgs& pa, int64_t N_shard, int64_t K, cudaStream_t s,
+                               unsigned flags) {
+    if (pa.world < 1 || pa.world > kMaxPeers || pa.rank < 0 || pa.rank >= pa.world)
+        return cudaErrorInvalidValue;
+    PeerOut po{};
+    for (int p = 0; p < pa.world; ++p) {
+        po.y[0][p] = static_cast<__half*>(pa.y[0][p]);
+        po.y[1][p] = static_cast<__half*>(pa.y[1][p]);
+        po.flag[p] = pa.flag[p];
+    }
+    po.row0 = pa.row0;
+    po.rank = pa.rank;
+    po.world = pa.world;
+    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, true>(W, scale, x, nullptr, N_shard, K, s,
+                                                          flags, po);
+}
+
+// Geometry chosen per call (measured on B200 with L2-cold pools):
+//  * independent GEMVs (CL_LAUNCH_PDL | CL_LAUNCH_INPUTS_READY): 4-warp CTAs,
+//    one per SM per GEMV, so up to four GEMVs overlap on an SM; 8-warp CTAs
+//    once K > 16384 (the staged activations then limit co-residency);
+//  * chained or plain launches: 8-warp CTAs, two per SM per GEMV (shorter
+//    per-GEMV latency), one per SM for K <= 2048.
+template <class Fmt>
+cudaError_t launch_mma_auto(const void* W, const void* scale, const void* x, void* y, int64_t N,
+                            int64_t K, cudaStream_t s, unsigned flags) {
+    if ((flags & 3u) == 3u)
+        return K <= 16384 ? launch_mma<Fmt, 4, 1>(W, scale, x, y, N, K, s, flags)
+                          : launch_mma<Fmt, 8, 1>(W, scale, x, y, N, K, s, flags);
+    return K <= 2048 ? launch_mma<Fmt, 8, 1>(W, scale, x, y, N, K, s, flags)
+                     : launch_mma<Fmt, 8, 2>(W, scale, x, y, N, K, s, flags);
+}
+
+template <class Fmt>
+cudaError_t launch_mma_sharded_auto(const void* W, const void* scale, const void* x,
+                                    const PeerArgs& pa, int64_t N, int64_t K, cudaStream_t s,
+                                    unsigned flags) {
+    if ((flags & 3u) == 3u)
+        return K <= 16384 ? launch_mma_sharded<Fmt, 4, 1>(W, scale, x, pa, N, K, s, flags)
+                          : launch_mma_sharded<Fmt, 8, 1>(W, scale, x, pa, N, K, s, flags);
+    return K <= 2048 ? launch_mma_sharded<Fmt, 8, 1>(W, scale, x, pa, N, K, s, flags)
+                     : launch_mma_sharded<Fmt, 8, 2>(W, scale, x, pa, N, K, s, flags);
 }
 
 const VariantDesc kInt4Variants[] = {
     {"int4gemv_baseline", launch_int4_scalar, false},
-    {"int4gemv_bulk", launch_vec<Int4Fmt, MathF16, true, 0>, false},
-    {"int4gemv_bulk_f32x2", launch_vec<Int4Fmt, MathF32x2, true, 1>, false},
-    {"int4gemv_ldg", launch_vec<Int4Fmt, MathF16, false, 2>, false},
-    {"int4gemv_ldg_f32x2", launch_vec<Int4Fmt, MathF32x2, false, 3>, false},
-    {"int4gemv_mma", launch_mma<MmaInt4, 8, 8>, false},
-    {"int4gemv_mma16", launch_mma<MmaInt4, 16, 10>, false},
+    {"int4gemv_bulk", launch_vec<Int4Fmt, MathF16, true>, false},
+    {"int4gemv_bulk_f32x2", launch_vec<Int4Fmt, MathF32x2, true>, false},
+    {"int4gemv_ldg", launch_vec<Int4Fmt, MathF16, false>, false},
+    {"int4gemv_ldg_f32x2", launch_vec<Int4Fmt, MathF32x2, false>, false},
+    {"int4gemv_mma", launch_mma_auto<MmaInt4>, false},
+    {"int4gemv_mma_w4", launch_mma<MmaInt4, 4, 1>, false},
+    {"int4gemv_mma_w8", launch_mma<MmaInt4, 8, 1>, false},
+    {"int4gemv_mma_w8c2", launch_mma<MmaInt4, 8, 2>, false},
+    {"int4gemv_mma_w16", launch_mma<MmaInt4, 16, 1>, false},
 };
 
 const VariantDesc kInt8Variants[] = {
     {"qgemv_baseline", launch_int8_scalar, false},
-    {"qgemv_bulk", launch_vec<Int8Fmt, MathF16, true, 4>, false},
-    {"qgemv_bulk_f32x2", launch_vec<Int8Fmt, MathF32x2, true, 5>, false},
-    {"qgemv_ldg", launch_vec<Int8Fmt, MathF16, false, 6>, false},
-    {"qgemv_ldg_f32x2", launch_vec<Int8Fmt, MathF32x2, false, 7>, false},
-    {"qgemv_mma", launch_mma<MmaInt8, 8, 9>, false},
-    {"qgemv_mma16", launch_mma<MmaInt8, 16, 11>, false},
+    {"qgemv_bulk", launch_vec<Int8Fmt, MathF16, true>, false},
+    {"qgemv_bulk_f32x2", launch_vec<Int8Fmt, MathF32x2, true>, false},
+    {"qgemv_ldg", launch_vec<Int8Fmt, MathF16, false>, false},
+    {"qgemv_ldg_f32x2", launch_vec<Int8Fmt, MathF32x2, false>, false},
+    {"qgemv_mma", launch_mma_auto<MmaInt8>, false},
+    {"qgemv_mma_w4", launch_mma<MmaInt8, 4, 1>, false},
+    {"qgemv_mma_w8", launch_mma<MmaInt8, 8, 1>, false},
+    {"qgemv_mma_w8c2", launch_mma<MmaInt8, 8, 2>, false},
+    {"qgemv_mma_w16", launch_mma<MmaInt8, 16, 1>, false},
 };
 
 }  // namespace
+
+const ShardedVariantDesc kInt4Sharded[] = {
+    {"int4gemv_mma", launch_mma_sharded_auto<MmaInt4>},
+    {"int4gemv_mma_w4", launch_mma_sharded<MmaInt4, 4, 1>},
+    {"int4gemv_mma_w8", launch_mma_sharded<MmaInt4, 8, 1>},
+    {"int4gemv_mma_w8c2", launch_mma_sharded<MmaInt4, 8, 2>},
+};
+
+const ShardedVariantDesc kInt8Sharded[] = {
+    {"qgemv_mma", launch_mma_sharded_auto<MmaInt8>},
+    {"qgemv_mma_w4", launch_mma_sharded<MmaInt8, 4, 1>},
+    {"qgemv_mma_w8", launch_mma_sharded<MmaInt8, 8, 1>},
+    {"qgemv_mma_w8c2", launch_mma_sharded<MmaInt8, 8, 2>},
+};
 
 const VariantDesc* int4_variants(int* count) {
     *count = (int)(sizeof(kInt4Variants) / sizeof(kInt4Variants[0]));
@@ -304,14 +392,24 @@ const VariantDesc* int8_variants(int* count) {
     return kInt8Variants;
 }
 
+const ShardedVariantDesc* int4_sharded_variants(int* count) {
+    *count = (int)(sizeof(kInt4Sharded) / sizeof(kInt4Sharded[0]));
+    return kInt4Sharded;
+}
+
+const ShardedVariantDesc* int8_sharded_variants(int* count) {
+    *count = (int)(sizeof(kInt8Sharded) / sizeof(kInt8Sharded[0]));
+    return kInt8Sharded;
+}
+
 cudaError_t read_device_status(int clear, int* status) {
     int v = 0, m = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&v, g_vec_status, sizeof(int));
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int));
 
     if (e != cudaSuccess) return e;
     if (clear) {
         const int zero = 0;
-        e = cudaMemcpyToSymbol(g_vec_status, &zero, sizeof(int));
+        e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
 
         if (e != cudaSuccess) return e;
     }

@@ -20,8 +20,29 @@ struct VariantDesc {
     bool quarantined;  // registered but not in the normal dispatch list
 };
 
+// Row-sharded GEMV with the all-gather fused into the epilogue: pointers (in
+// this process) to every rank's two y buffers (by step parity) and flag block
+// (16 words), and the shard's first row.
+struct PeerArgs {
+    void* y[2][8];
+    unsigned* flag[8];
+    int64_t row0;
+    int rank, world;
+};
+
+using ShardedLaunchFn = cudaError_t (*)(const void* W, const void* scale, const void* x,
+                                        const PeerArgs& peers, int64_t N_shard, int64_t K,
+                                        cudaStream_t stream, unsigned flags);
+
+struct ShardedVariantDesc {
+    const char* name;
+    ShardedLaunchFn fn;
+};
+
 const VariantDesc* int4_variants(int* count);
 const VariantDesc* int8_variants(int* count);
+const ShardedVariantDesc* int4_sharded_variants(int* count);
+const ShardedVariantDesc* int8_sharded_variants(int* count);
 
 // Reads (optionally clears) the device-side bounded-wait status word of the
 // current device.

@@ -9,9 +9,8 @@
 // nearly all that remains.
 //
 // Decomposition
-//   * Each CTA owns a balanced, contiguous range of rows (1-row granularity).
-//   * Rows form 16-row mma tiles (the last one partial; missing rows are
-//     never fetched).  A row is cut into 64-byte blocks (INT4: one 128-wide
+//   * Each CTA owns a balanced, contiguous range of 16-row mma tiles (only the
+//     matrix's last tile can be partial; its missing rows are never fetched).  A row is cut into 64-byte blocks (INT4: one 128-wide
 //     scale group; INT8: 64 elements) and blocks into chunks of 4.
 //   * An item = (tile, chunk) = 16 rows x 256 bytes.  Warp w processes items
 //     w, w+8, ... .  Lane (g, t) loads its A fragments directly from global
@@ -47,7 +46,7 @@ struct MmaGeom {
     int64_t row_bytes;  // RB
     int32_t blocks;     // NB = RB / 64
     int32_t n_kc;       // chunks per row = ceil(NB / 4)
-    int32_t rows_base, rows_rem, ctas;
+    int32_t tiles_base, tiles_rem, ctas;  // 16-row tiles per CTA (balanced)
     int32_t xs_bytes;   // staged activations (K halves)
     int32_t max_items;  // items of the largest CTA
     int32_t max_rows;   // rows of the largest CTA
@@ -92,59 +91,56 @@ __device__ __forceinline__ uint2 lds8(uint32_t addr) {
     return v;
 }
 
+// Formats.  kAcc: independent accumulators per item (blocks of even / odd
+// index), which halves the length of the dependent mma chain.
 struct MmaInt4 {
     static constexpr int kSteps = 8;  // k-steps per 64-byte block (128 elements)
     static constexpr bool kGroupScale = true;
+    static constexpr int kBlockWords = 16;  // uint4 words of x per block
+    static constexpr int kAcc = 2;
     using Scale = __half;
 };
 struct MmaInt8 {
     static constexpr int kSteps = 4;  // 64 elements
     static constexpr bool kGroupScale = false;
+    static constexpr int kBlockWords = 8;
+    static constexpr int kAcc = 2;
     using Scale = float;
 };
-
-
-// Accumulate one 64-byte block of rows g (wa) and g+8 (wb) into d.  `bp`
-// points at the block's staged activations for the lanes of the batch column
-// that this block feeds, and at a zero region for every other lane, so all
-// lanes load unconditionally.  One 16-byte load covers two k-steps.
+// Accumulate one 64-byte block (index q inside its item) of rows g (wa) and
+// g+8 (wb).  `bp` points at the block's staged activations for the lanes of
+// the batch column that this block feeds, and at a zero region for every
+// other lane, so all lanes load unconditionally.  One 16-byte load covers two
+// k-steps.
 template <class Fmt>
 __device__ __forceinline__ void mma_block(const uint4 wa, const uint4 wb, const uint4* bp, int t,
-                                          float (&d)[4]);
-
-template <>
-__device__ __forceinline__ void mma_block<MmaInt4>(const uint4 wa, const uint4 wb,
-                                                   const uint4* bp, int t, float (&d)[4]) {
+                                          int q, float (&acc)[Fmt::kAcc][4]) {
     const uint32_t ua[4] = {wa.x, wa.y, wa.z, wa.w};
     const uint32_t ub[4] = {wb.x, wb.y, wb.z, wb.w};
+    if constexpr (Fmt::kGroupScale) {
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const uint4 bb = bp[w * 4 + t];  // steps 2w (x, y) and 2w+1 (z, w)
-        // operands of one step are produced back to back, in quad order
-        mma_16816(d, nib_pair_lo(ua[w]), nib_pair_lo(ub[w]), nib_pair_hi(ua[w]),
-                  nib_pair_hi(ub[w]), bb.x, bb.y);
-        const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
-        mma_16816(d, nib_pair_lo(ha), nib_pair_lo(hb), nib_pair_hi(ha), nib_pair_hi(hb), bb.z,
-                  bb.w);
-    }
-}
-
-template <>
-__device__ __forceinline__ void mma_block<MmaInt8>(const uint4 wa, const uint4 wb,
-                                                   const uint4* bp, int t, float (&d)[4]) {
-    const uint32_t ua[4] = {wa.x, wa.y, wa.z, wa.w};
-    const uint32_t ub[4] = {wb.x, wb.y, wb.z, wb.w};
+        for (int w = 0; w < 4; ++w) {
+            const uint4 bb = bp[w * 4 + t];  // (x0,x4) (x1,x5) (x2,x6) (x3,x7) of word w
+            const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
+            // operands of one step are produced back to back, in quad order
+            mma_16816(acc[q & 1], nib_pair_lo(ua[w]), nib_pair_lo(ub[w]), nib_pair_hi(ua[w]),
+                      nib_pair_hi(ub[w]), bb.x, bb.y);
+            mma_16816(acc[q & 1], nib_pair_lo(ha), nib_pair_lo(hb), nib_pair_hi(ha),
+                      nib_pair_hi(hb), bb.z, bb.w);
+        }
+    } else {
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-        const uint4 bb = bp[2 * t + jj];  // x[16t + 8jj .. +8): steps 2jj and 2jj+1
+        for (int jj = 0; jj < 2; ++jj) {
+            const uint4 bb = bp[2 * t + jj];  // x[16t + 8jj .. +8): steps 2jj and 2jj+1
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int j = 2 * jj + h;
-            __half2 qa[2], qb[2];
-            int8x4_to_h2(ua[j], qa);
-            int8x4_to_h2(ub[j], qb);
-            mma_16816(d, h2_as_u32(qa[0]), h2_as_u32(qb[0]), h2_as_u32(qa[1]), h2_as_u32(qb[1]),
-                      h ? bb.z : bb.x, h ? bb.w : bb.y);
+            for (int h = 0; h < 2; ++h) {
+                const int j = 2 * jj + h;
+                __half2 qa[2], qb[2];
+                int8x4_to_h2(ua[j], qa);
+                int8x4_to_h2(ub[j], qb);
+                mma_16816(acc[q & 1], h2_as_u32(qa[0]), h2_as_u32(qb[0]), h2_as_u32(qa[1]),
+                          h2_as_u32(qb[1]), h ? bb.z : bb.x, h ? bb.w : bb.y);
+            }
         }
     }
 }
@@ -205,39 +201,46 @@ __device__ __forceinline__ void mma_fetch(MmaItemRegs& r, const uint8_t* W,
 }
 
 // Compute one item and store its two row partials (rows g, g+8 of the tile).
-// INT4: block q of the item is fed through batch column q, so one
-// accumulator keeps the four blocks' sums apart (columns 2t, 2t+1 in lane t);
-// the group scales are applied once per item, then the two lanes holding a
-// row's columns are combined.  INT8: all blocks share column 0 (the row
-// scale is applied at the very end).
+// INT4: block q of the item is fed through batch column q, so the
+// accumulators keep the four blocks' sums apart (columns 2t, 2t+1 in lane t;
+// a block's column is non-zero only in the accumulator of its parity); the
+// group scales are applied once per item, then the two lanes holding a row's
+// columns are combined.  INT8: all blocks share column 0 (the row scale is
+// applied at the very end).
 template <class Fmt, bool kFull>
 __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs,
-                                           const uint4* zero, MmaCursor c, const MmaGeom& g,
-                                           int gq, int t, float* part) {
+                                           const uint4* zero, MmaCursor c,
+                                           const MmaGeom& g, int gq, int t, float* part) {
     const int nb =
         kFull ? kMmaChunkBlocks : min(kMmaChunkBlocks, g.blocks - kMmaChunkBlocks * c.kc);
-    constexpr int kBlk = Fmt::kGroupScale ? 16 : 8;  // uint4 per block of staged activations
-    const uint4* xbase = xs + kMmaChunkBlocks * c.kc * kBlk;
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    constexpr int kBlk = Fmt::kBlockWords;  // uint4 per block of staged activations
+    const int blk0 = kMmaChunkBlocks * c.kc;
+    const uint4* xbase = xs + blk0 * kBlk;
+    float acc[Fmt::kAcc][4];
+#pragma unroll
+    for (int i = 0; i < Fmt::kAcc; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll
     for (int q = 0; q < kMmaChunkBlocks; ++q) {
         if (kFull || q < nb) {
             const int col = Fmt::kGroupScale ? q : 0;
             const uint4* bp = gq == col ? xbase + q * kBlk : zero;
-            mma_block<Fmt>(r.wa[q], r.wb[q], bp, t, d);
+            mma_block<Fmt>(r.wa[q], r.wb[q], bp, t, q, acc);
         }
     }
     float acc_a, acc_b;
     if constexpr (Fmt::kGroupScale) {
-        // lane t < 2 holds columns (blocks) 2t, 2t+1; lanes t >= 2 hold zero columns
-        acc_a = fmaf(__half2float(r.sa[1]), d[1], __half2float(r.sa[0]) * d[0]);
-        acc_b = fmaf(__half2float(r.sb[1]), d[3], __half2float(r.sb[0]) * d[2]);
+        // lane t < 2 holds columns (blocks) 2t (even accumulator, entries 0 / 2)
+        // and 2t + 1 (odd accumulator, entries 1 / 3); lanes t >= 2 hold zero columns
+        const float sa0 = __half2float(r.sa[0]), sa1 = __half2float(r.sa[1]);
+        const float sb0 = __half2float(r.sb[0]), sb1 = __half2float(r.sb[1]);
+        acc_a = fmaf(sa1, acc[1][1], sa0 * acc[0][0]);
+        acc_b = fmaf(sb1, acc[1][3], sb0 * acc[0][2]);
         if (t >= 2) acc_a = acc_b = 0.f;
         acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
         acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
     } else {
-        acc_a = d[0];
-        acc_b = d[2];
+        acc_a = acc[0][0] + acc[1][0];
+        acc_b = acc[0][2] + acc[1][2];
     }
     if (t == 0) {
         float* pp = part + (c.tile * g.n_kc + c.kc) * 16;
@@ -258,23 +261,91 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
 
 constexpr int kZeroRegion = 256;  // bytes of zeros ahead of the staged activations
 
-// kWarps = 8: two CTAs fit on an SM (room for the next kernel's CTA under
-// programmatic dependent launch); kWarps = 16: one CTA per SM, twice the
-// warps in flight.
-template <class Fmt, int kWarps, bool kAllFull>
-__global__ void __launch_bounds__(32 * kWarps, kWarps == 8 ? 2 : 1)
+// ---------------------------------------------------------------------------
+// Row-sharded GEMV with the all-gather fused into the epilogue.
+//
+// Every rank owns a contiguous shard of the rows of W.  Instead of writing its
+// y rows locally and running a separate all-gather, each CTA stores its rows
+// straight into the y buffer of every rank (peer pointers over NVLink), so
+// the exchange overlaps the other CTAs' compute.  Each rank's flag block
+// holds: [0, kMaxPeers) the last step each rank has completed writing into
+// this rank's buffers, [kTicket] the CTA arrival counter of the running step,
+// [kStep] the last step this rank completed.  Per step:
+//   0. after the preceding kernel completed, the CTA reads the step number
+//      e = flag[kStep] + 1 (so a captured graph replays correctly);
+//   1. it stores its rows into y[e & 1] of every rank, fences at system scope,
+//      syncs and takes a ticket;
+//   2. the CTA holding the last ticket resets the ticket, fences, and writes
+//      e into slot [rank] of every rank's flag block (release);
+//   3. that CTA waits (bounded) until every slot of its own flag block is at
+//      least e (acquire), then records flag[kStep] = e; when the grid
+//      completes, y[e & 1] holds all rows.
+// A rank can run at most one step ahead of another (step e+1 cannot complete
+// before every rank started it, i.e. finished step e), so with two y buffers
+// alternating by step parity a buffer is never rewritten while a lagging
+// rank still reads it.  Only plain peer loads and stores are used.
+// ---------------------------------------------------------------------------
+constexpr int kMaxPeers = 8;
+constexpr int kFlagWords = 16;  // words per rank's flag block
+constexpr int kTicket = kMaxPeers;
+constexpr int kStep = kMaxPeers + 1;
+
+struct PeerOut {
+    __half* y[2][kMaxPeers];    // y buffers of every rank, by step parity and rank
+    unsigned* flag[kMaxPeers];  // flag block of every rank, by rank
+    int64_t row0;               // first row of this rank's shard in y
+    int rank, world;
+};
+
+// Called by thread 0 of every CTA after a CTA barrier that follows the CTA's
+// peer stores: the system-scope fence before the ticket publishes the whole
+// CTA's stores (cumulativity through the barrier); the last CTA's fence and
+// release stores publish every CTA's stores (through the ticket atomics).
+// Loops run over the compile-time peer slots so that `po` stays in the
+// parameter space (no local copy).
+__device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned epoch) {
+    unsigned* mine = po.flag[po.rank];
+    __threadfence_system();
+    const unsigned prev = atomicAdd(mine + kTicket, 1u);
+    if (prev != gridDim.x - 1) return;
+    atomicExch(mine + kTicket, 0u);
+    __threadfence_system();
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+        if (p < po.world) st_release_sys(po.flag[p] + po.rank, epoch);
+    const long long t0 = clock64();
+    bool ok = true;
+    for (int q = 0; q < po.world && ok; ++q) {
+        while ((int)(ld_acquire_sys(mine + q) - epoch) < 0) {
+            if (clock64() - t0 > kWaitTimeoutCycles) {
+                record_status(kStatusTimeoutPeer);
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    atomicExch(mine + kStep, epoch);
+}
+
+// kPeer: y is ignored; rows go to every rank's buffer in `po` (see PeerOut).
+template <class Fmt, int kWarps, bool kAllFull, bool kPeer>
+__global__ void __launch_bounds__(32 * kWarps, 16 / kWarps)
 gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __restrict__ scale,
-                const __half* __restrict__ x, __half* __restrict__ y, const MmaGeom g) {
+                const __half* __restrict__ x, __half* __restrict__ y, const MmaGeom g,
+                const PeerOut po) {
     constexpr int kThreads = 32 * kWarps;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* xs = smem + kZeroRegion;
     float* part = reinterpret_cast<float*>(smem + mma_part_off(g));
     float* sc8 = reinterpret_cast<float*>(smem + mma_sc_off(g));
 
+    // Whole 16-row tiles per CTA; only the matrix's last tile can be partial.
     const int b = blockIdx.x;
-    const int64_t r0 = (int64_t)b * g.rows_base + (b < g.rows_rem ? b : g.rows_rem);
-    const int nrows = g.rows_base + (b < g.rows_rem ? 1 : 0);
-    const int n_tiles = (nrows + 15) >> 4;
+    const int n_tiles = g.tiles_base + (b < g.tiles_rem ? 1 : 0);
+    const int64_t r0 = 16 * ((int64_t)b * g.tiles_base + (b < g.tiles_rem ? b : g.tiles_rem));
+    const int64_t left = g.N - r0;
+    const int nrows = left < 16 * n_tiles ? (int)left : 16 * n_tiles;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gq = lane >> 2, t = lane & 3;
     const uint64_t pol = policy_evict_first();
@@ -338,6 +409,14 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     __syncthreads();
     // y may be read or written by the preceding kernel: store only after it.
     if (g.early_x) pdl_wait_prior_grids();
+    unsigned epoch = 0;
+    if constexpr (kPeer) {
+        // the step number, written by the preceding step's last CTA (complete now)
+        __shared__ unsigned s_epoch;
+        if (tid == 0) s_epoch = *reinterpret_cast<volatile unsigned*>(po.flag[po.rank] + kStep) + 1u;
+        __syncthreads();
+        epoch = s_epoch;
+    }
     // ---- per-row sums over chunks, in chunk order ----
     for (int r = tid; r < nrows; r += kThreads) {
         const int tile = r >> 4, rr = r & 15;
@@ -345,7 +424,19 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
         float s = 0.f;
         for (int kc = 0; kc < g.n_kc; ++kc) s += pp[kc * 16];
         if constexpr (!Fmt::kGroupScale) s *= sc8[r];
-        y[r0 + r] = __float2half_rn(s);
+        const __half h = __float2half_rn(s);
+        if constexpr (kPeer) {
+            const int64_t row = po.row0 + r0 + r;
+#pragma unroll
+            for (int p = 0; p < kMaxPeers; ++p)
+                if (p < po.world) ((epoch & 1) ? po.y[1][p] : po.y[0][p])[row] = h;
+        } else {
+            y[r0 + r] = h;
+        }
+    }
+    if constexpr (kPeer) {
+        __syncthreads();
+        if (tid == 0) peer_arrive_and_wait(po, epoch);
     }
 }
 

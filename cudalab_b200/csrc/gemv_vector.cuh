@@ -318,12 +318,6 @@ __device__ __forceinline__ float warp_reduce4(float v0, float v1, float v2, floa
     return c;
 }
 
-// Per-device status word for bounded waits (one per translation unit that
-// includes this header; read through the C ABI).
-static __device__ int g_vec_status;
-
-__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_vec_status, 0, code); }
-
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------

@@ -119,6 +119,52 @@ int cl_qgemv_native_timing(const char* variant, const int8_t* W_q, const float* 
  * kernels/qgemv/bindings.cpp:281-306. */
 int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
 
+/* ---- row-sharded GEMV over the GPUs of one node (one process per GPU) ----
+ *
+ * Rows of W are split into contiguous shards, one per rank; x is replicated;
+ * every rank ends the step holding all N_total rows of y.  Replaces the
+ * "local GEMV, then NCCL all-gather of y" step of the reference's sharded
+ * configuration (70B-class MLP shapes; the reference has no multi-GPU code,
+ * so there is no reference entry point): here the all-gather is fused into
+ * the GEMV epilogue, each CTA storing its rows into every rank's y buffer
+ * over NVLink peer mappings and the ranks completing the step through a flag
+ * block (no multicast objects are used). */
+#define CL_MAX_PEERS 8
+#define CL_IPC_HANDLE_BYTES 64
+#define CL_PEER_FLAG_BYTES 64 /* size of one rank's flag block (zeroed at allocation) */
+
+/* Allocates `bytes` of device memory on the current device, zero-filled, and
+ * writes its CUDA IPC handle (CL_IPC_HANDLE_BYTES bytes) to ipc_handle.  Setup
+ * only: the GEMV entry points never allocate. */
+int cl_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Maps another process's cl_peer_alloc buffer into this process. */
+int cl_peer_open(const void* ipc_handle, void** peer_ptr);
+int cl_peer_close(void* peer_ptr);
+int cl_peer_free(void* ptr);
+
+/* One step of the sharded INT4 GEMV on this rank.
+ *   W_shard [N_shard, K/2], scale_shard [N_shard, K/128]: rows
+ *     [row0, row0 + N_shard) of the full matrix; x [K] (same on every rank).
+ *   y_peers[2 * world]: every rank's two y buffers (N_total halves each) as
+ *     pointers valid in this process, parity-0 buffers of ranks 0..world-1
+ *     first, then the parity-1 buffers (own rank: local pointers).
+ *   flag_peers[world]: every rank's flag block (CL_PEER_FLAG_BYTES, zero
+ *     before the first step).
+ * Step e (1, 2, ... counted on the device, so the call can be captured into a
+ * CUDA graph) writes the parity (e & 1) buffers.  All ranks must issue the
+ * same steps in the same order.  A rank that waits more than about two
+ * seconds for another records status 5 (cl_device_status) instead of
+ * hanging; the group must then be set up again. */
+int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void* scale_shard,
+                        const void* x, void* const* y_peers, void* const* flag_peers, int rank,
+                        int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
+                        void* stream, uint32_t flags);
+/* Same for INT8 (W_shard int8 [N_shard, K], scale_shard fp32 [N_shard], K % 64 == 0). */
+int cl_qgemv_sharded(const char* variant, const int8_t* W_shard, const float* scale_shard,
+                     const void* x, void* const* y_peers, void* const* flag_peers, int rank,
+                     int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
+                     void* stream, uint32_t flags);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -66,7 +66,8 @@ FULL = [(4096, 4096), (1024, 4096), (4096, 1024), (11008, 4096), (4096, 11008)]
 
 
 @pytest.mark.parametrize("shape", FULL, ids=lambda s: f"{s[0]}x{s[1]}")
-@pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_bulk", "int4gemv_ldg"])
+@pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_mma_w4", "int4gemv_mma_w8c2",
+                                     "int4gemv_bulk", "int4gemv_ldg"])
 def test_full_size_vs_oracle(ext, variant, shape):
     N, K = shape
     Wp, s, _ = make_w4(N, K, seed=77, scale=0.02)
@@ -130,3 +131,64 @@ def test_native_timing(ext):
     assert set(d) >= {"variant", "median_us", "min_us", "max_us", "mean_us", "window_median_us"}
     assert len(d["window_median_us"]) == 3 and 0 < d["min_us"] <= d["max_us"] < 1e5
     assert nat.device_status(clear=True) == 0
+
+
+def _outlier_case(N, K, seed):
+    """Groups whose quantised values are nearly all 0 (one outlier of about
+    +-5 among weights of about 1e-3) and activations spread over six decades:
+    the inputs on which a biased tensor-core operand loses the most relative
+    accuracy."""
+    g = torch.Generator().manual_seed(seed)
+    W = torch.randn(N, K, generator=g) * 1e-3
+    idx = torch.randint(0, 128, (N, K // 128), generator=g) + torch.arange(0, K, 128)
+    W.scatter_(1, idx, torch.randn(N, K // 128, generator=g).sign() * 5.0)
+    mag = torch.pow(10.0, torch.randint(-3, 3, (K,), generator=g).float())
+    x = (torch.randn(K, generator=g) * mag).half()
+    from cudalab_b200.int4gemv_quantize import quantize_w
+    Wp, s = quantize_w(W.half())
+    return Wp.cuda(), s.cuda(), x.cuda()
+
+
+@pytest.mark.parametrize("K", [128, 1024, 4096])
+@pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_mma_w4", "int4gemv_mma_w8",
+                                     "int4gemv_mma_w8c2", "int4gemv_mma_w16",
+                                     "int4gemv_baseline"])
+def test_outlier_groups_vs_oracle(ext, variant, K):
+    Wp, s, x = _outlier_case(512, K, seed=K)
+    y = ext.forward(variant, Wp, s, x).cpu().numpy()
+    r = orc.check(y, Wp.cpu().numpy(), s.cpu().numpy(), x.cpu().numpy())
+    assert r["pass"], r
+
+
+@pytest.fixture(scope="module")
+def one_rank_group():
+    import torch.distributed as dist
+    if dist.is_initialized():
+        yield None
+        return
+    store = dist.HashStore()
+    dist.init_process_group("gloo", store=store, rank=0, world_size=1)
+    yield None
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("flags", [0, 1, 3])
+@pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_mma_w4", "int4gemv_mma_w8",
+                                     "int4gemv_mma_w8c2"])
+def test_sharded_fused_single_rank(ext, one_rank_group, variant, flags):
+    """The fused sharded step with one rank (the peer epilogue, the flag
+    protocol and the device step counter on a single GPU) equals the plain
+    GEMV bit for bit over several steps."""
+    from cudalab_b200.sharded import ShardedGemv
+    Wp, s, _ = make_w4(1000, 2048, seed=3)
+    sg = ShardedGemv("int4gemv", Wp, s, 1000, 2048, variant=variant, mode="fused")
+    try:
+        for step in range(4):
+            x = make_x4(2048, seed=50 + step)
+            y = sg.forward(x, flags=flags).clone()
+            ref = ext.forward(variant, Wp, s, x)
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref), step
+        assert nat.device_status(clear=True) == 0
+    finally:
+        sg.close()

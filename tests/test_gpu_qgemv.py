@@ -56,7 +56,8 @@ def test_golden_vectors(ext, variant):
 
 @pytest.mark.parametrize("shape", [(4096, 4096), (11008, 4096), (4096, 11008), (4096, 1024)],
                          ids=lambda s: f"{s[0]}x{s[1]}")
-@pytest.mark.parametrize("variant", ["qgemv_mma", "qgemv_bulk", "qgemv_ldg"])
+@pytest.mark.parametrize("variant", ["qgemv_mma", "qgemv_mma_w4", "qgemv_mma_w8c2", "qgemv_bulk",
+                                     "qgemv_ldg"])
 def test_full_size_vs_oracle(ext, variant, shape):
     N, K = shape
     Wq, s, _ = make_w_q(N, K, seed=17, scale=0.02)
@@ -76,3 +77,22 @@ def test_deterministic_and_pdl_identical(ext, variant):
     y3 = ext.forward(variant, Wq, s, x, flags=nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY)
     assert torch.equal(y0, y1) and torch.equal(y0, y2) and torch.equal(y0, y3)
     assert nat.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("K", [64, 1024, 4096])
+@pytest.mark.parametrize("variant", ["qgemv_mma", "qgemv_mma_w4", "qgemv_mma_w8", "qgemv_mma_w8c2",
+                                     "qgemv_mma_w16", "qgemv_baseline"])
+def test_outlier_rows_vs_oracle(ext, variant, K):
+    """Rows with one large weight among tiny ones (quantised values nearly all
+    0) and activations spread over six decades."""
+    g = torch.Generator().manual_seed(K)
+    N = 512
+    W = torch.randn(N, K, generator=g) * 1e-3
+    W[torch.arange(N), torch.randint(0, K, (N,), generator=g)] = 5.0
+    mag = torch.pow(10.0, torch.randint(-3, 3, (K,), generator=g).float())
+    x = (torch.randn(K, generator=g) * mag).half()
+    from cudalab_b200.qgemv_quantize import quantize_w
+    Wq, s = quantize_w(W.half())
+    y = ext.forward(variant, Wq.cuda(), s.cuda(), x.cuda()).cpu().numpy()
+    r = orc.check(y, Wq.numpy(), s.numpy(), x.numpy())
+    assert r["pass"], r
