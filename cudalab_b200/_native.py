@@ -55,10 +55,12 @@ PROTOTYPES = {
     "cl_peer_open": (_int, [_vp, ctypes.POINTER(_vp)]),
     "cl_peer_close": (_int, [_vp]),
     "cl_peer_free": (_int, [_vp]),
-    "cl_int4gemv_sharded": (_int, [_cs, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64,
-                                   _i64, _vp, _u32]),
-    "cl_qgemv_sharded": (_int, [_cs, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64,
-                                _i64, _vp, _u32]),
+    "cl_int4gemv_sharded": (_int, [_cs, _vp, _vp, _vp, _i64, _vp, _vp, _int, _int, _i64, _i64,
+                                   _i64, _i64, _vp, _u32]),
+    "cl_qgemv_sharded": (_int, [_cs, _vp, _vp, _vp, _i64, _vp, _vp, _int, _int, _i64, _i64,
+                                _i64, _i64, _vp, _u32]),
+    "cl_int4gemv_batched": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u32]),
+    "cl_qgemv_batched": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u32]),
 }
 
 CL_MAX_PEERS = 8

@@ -94,8 +94,30 @@ int run(const clb::VariantDesc* table, int n, const char* op, const char* varian
     if (!v) return fail(CL_ERR_UNKNOWN_VARIANT, unknown_msg(op, table, n, variant));
     const int rc = check_args(op, W, scale, x, out, N, K, is_int4);
     if (rc != CL_OK) return rc;
-    cudaError_t e = v->fn(W, scale, x, out, N, K, static_cast<cudaStream_t>(stream), flags);
+    const clb::GemvArgs a{W, scale, x, out, N, K, 1, K, N};
+    cudaError_t e = v->fn(a, static_cast<cudaStream_t>(stream), flags);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    return CL_OK;
+}
+
+// Batched: X [M, K] -> Y [M, N], both row-major and contiguous; the
+// tensor-core kernels take up to 16 activation rows per launch.
+int run_batched(const clb::VariantDesc* table, int n, const char* op, const char* variant,
+                const void* W, const void* scale, const void* X, void* Y, int64_t M, int64_t N,
+                int64_t K, void* stream, uint32_t flags, bool is_int4) {
+    const clb::VariantDesc* v = find(table, n, variant);
+    if (!v) return fail(CL_ERR_UNKNOWN_VARIANT, unknown_msg(op, table, n, variant));
+    if (M <= 0) return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": M must be > 0");
+    const int rc = check_args(op, W, scale, X, Y, N, K, is_int4);
+    if (rc != CL_OK) return rc;
+    constexpr int64_t kPass = 16;
+    for (int64_t m0 = 0; m0 < M; m0 += kPass) {
+        const clb::GemvArgs a{W, scale, static_cast<const uint16_t*>(X) + m0 * K,
+                              static_cast<uint16_t*>(Y) + m0 * N, N, K,
+                              std::min<int64_t>(kPass, M - m0), K, N};
+        cudaError_t e = v->fn(a, static_cast<cudaStream_t>(stream), flags);
+        if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    }
     return CL_OK;
 }
 
@@ -112,8 +134,9 @@ int timing(const clb::VariantDesc* table, int n, const char* op, const char* var
     int rc = check_args(op, W, scale, x, out, N, K, is_int4);
     if (rc != CL_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+    const clb::GemvArgs a{W, scale, x, out, N, K, 1, K, N};
     for (int64_t i = 0; i < warmup; ++i) {
-        cudaError_t e = v->fn(W, scale, x, out, N, K, s, flags);
+        cudaError_t e = v->fn(a, s, flags);
         if (e != cudaSuccess) return cuda_fail(e, "warmup launch");
     }
     cudaError_t e = cudaStreamSynchronize(s);
@@ -128,7 +151,7 @@ int timing(const clb::VariantDesc* table, int n, const char* op, const char* var
     for (int64_t w = 0; w < n_windows && rc == CL_OK; ++w) {
         if ((e = cudaEventRecord(ev0, s)) != cudaSuccess) { rc = cuda_fail(e, "event record"); break; }
         for (int64_t i = 0; i < lpw; ++i) {
-            e = v->fn(W, scale, x, out, N, K, s, flags);
+            e = v->fn(a, s, flags);
             if (e != cudaSuccess) { rc = cuda_fail(e, "timed launch"); break; }
         }
         if (rc != CL_OK) break;
@@ -152,7 +175,7 @@ const clb::ShardedVariantDesc* find_sharded(const clb::ShardedVariantDesc* t, in
 }
 
 int run_sharded(const clb::ShardedVariantDesc* table, int n, const char* op, const char* variant,
-                const void* W, const void* scale, const void* x, void* const* y_peers,
+                const void* W, const void* scale, const void* x, int64_t M, void* const* y_peers,
                 void* const* flag_peers, int rank, int world, int64_t row0, int64_t N_shard,
                 int64_t N_total, int64_t K, void* stream, uint32_t flags, bool is_int4) {
     const std::string o(op);
@@ -165,6 +188,8 @@ int run_sharded(const clb::ShardedVariantDesc* table, int n, const char* op, con
     }
     int rc = check_args(op, W, scale, x, y_peers, N_shard, K, is_int4);
     if (rc != CL_OK) return rc;
+    if (M < 1 || M > 16)
+        return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: M must be in [1, 16]");
     if (world < 1 || world > CL_MAX_PEERS)
         return fail(CL_ERR_INVALID_ARGUMENT, o + "_sharded: world must be in [1, 8]");
     if (rank < 0 || rank >= world)
@@ -187,7 +212,8 @@ int run_sharded(const clb::ShardedVariantDesc* table, int n, const char* op, con
     pa.row0 = row0;
     pa.rank = rank;
     pa.world = world;
-    cudaError_t e = v->fn(W, scale, x, pa, N_shard, K, static_cast<cudaStream_t>(stream), flags);
+    const clb::GemvArgs a{W, scale, x, nullptr, N_shard, K, M, K, N_total};
+    cudaError_t e = v->fn(a, pa, static_cast<cudaStream_t>(stream), flags);
     if (e != cudaSuccess) {
         char ctx[160];
         std::snprintf(ctx, sizeof ctx, "sharded kernel launch (rank %d/%d, rows %lld+%lld of %lld, K %lld)",
@@ -226,6 +252,15 @@ int cl_int4gemv(const char* variant, const uint8_t* W_packed, const void* scale,
     return cl_int4gemv_ex(variant, W_packed, scale, x, out, N, K, stream, 0u);
 }
 
+int cl_int4gemv_batched(const char* variant, const uint8_t* W_packed, const void* scale,
+                        const void* X, void* Y, int64_t M, int64_t N, int64_t K, void* stream,
+                        uint32_t flags) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int4_variants(&n);
+    return run_batched(t, n, "int4gemv", variant, W_packed, scale, X, Y, M, N, K, stream, flags,
+                       true);
+}
+
 int cl_int4gemv_native_timing(const char* variant, const uint8_t* W_packed, const void* scale,
                               const void* x, void* out, int64_t N, int64_t K, int64_t warmup,
                               int64_t n_windows, int64_t launches_per_window, void* stream,
@@ -253,6 +288,13 @@ int cl_qgemv_ex(const char* variant, const int8_t* W_q, const float* scale, cons
 int cl_qgemv(const char* variant, const int8_t* W_q, const float* scale, const void* x, void* out,
              int64_t N, int64_t K, void* stream) {
     return cl_qgemv_ex(variant, W_q, scale, x, out, N, K, stream, 0u);
+}
+
+int cl_qgemv_batched(const char* variant, const int8_t* W_q, const float* scale, const void* X,
+                     void* Y, int64_t M, int64_t N, int64_t K, void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int8_variants(&n);
+    return run_batched(t, n, "qgemv", variant, W_q, scale, X, Y, M, N, K, stream, flags, false);
 }
 
 int cl_qgemv_native_timing(const char* variant, const int8_t* W_q, const float* scale,
@@ -317,22 +359,24 @@ int cl_peer_free(void* ptr) {
 }
 
 int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void* scale_shard,
-                        const void* x, void* const* y_peers, void* const* flag_peers, int rank,
+                        const void* x, int64_t M, void* const* y_peers, void* const* flag_peers,
+                        int rank,
                         int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
                         void* stream, uint32_t flags) {
     int n = 0;
     const clb::ShardedVariantDesc* t = clb::int4_sharded_variants(&n);
-    return run_sharded(t, n, "int4gemv", variant, W_shard, scale_shard, x, y_peers, flag_peers,
+    return run_sharded(t, n, "int4gemv", variant, W_shard, scale_shard, x, M, y_peers, flag_peers,
                        rank, world, row0, N_shard, N_total, K, stream, flags, true);
 }
 
 int cl_qgemv_sharded(const char* variant, const int8_t* W_shard, const float* scale_shard,
-                     const void* x, void* const* y_peers, void* const* flag_peers, int rank,
+                     const void* x, int64_t M, void* const* y_peers, void* const* flag_peers,
+                     int rank,
                      int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
                      void* stream, uint32_t flags) {
     int n = 0;
     const clb::ShardedVariantDesc* t = clb::int8_sharded_variants(&n);
-    return run_sharded(t, n, "qgemv", variant, W_shard, scale_shard, x, y_peers, flag_peers,
+    return run_sharded(t, n, "qgemv", variant, W_shard, scale_shard, x, M, y_peers, flag_peers,
                        rank, world, row0, N_shard, N_total, K, stream, flags, false);
 }
 

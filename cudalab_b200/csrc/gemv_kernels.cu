@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "gemv_launch.h"
@@ -163,29 +164,38 @@ GemvGeom make_geom(int64_t N, int64_t K, bool int4, bool bulk, int num_sms) {
 
 template <class Kern, class... Args>
 cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                   unsigned flags, Args... args) {
+                   unsigned flags, int cluster, Args... args) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    cfg.numAttrs = 0;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
     if (flags & 1u) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
     }
+    if (cluster > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = (unsigned)cluster;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = n ? attr : nullptr;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---- scalar and CUDA-core kernels: one activation row per launch ----
 cudaError_t launch_int4_scalar(const void* W, const void* scale, const void* x, void* y, int64_t N,
                                int64_t K, cudaStream_t s, unsigned flags) {
     const dim3 grid((unsigned)((N + 7) / 8));
-    return launch(int4gemv_scalar_kernel, grid, dim3(256), 0, s, flags,
+    return launch(int4gemv_scalar_kernel, grid, dim3(256), 0, s, flags, 1,
                   static_cast<const uint8_t*>(W), static_cast<const __half*>(scale),
                   static_cast<const __half*>(x), static_cast<__half*>(y), N, K);
 }
@@ -193,14 +203,14 @@ cudaError_t launch_int4_scalar(const void* W, const void* scale, const void* x, 
 cudaError_t launch_int8_scalar(const void* W, const void* scale, const void* x, void* y, int64_t N,
                                int64_t K, cudaStream_t s, unsigned flags) {
     const dim3 grid((unsigned)((N + 7) / 8));
-    return launch(qgemv_scalar_kernel, grid, dim3(256), 0, s, flags,
+    return launch(qgemv_scalar_kernel, grid, dim3(256), 0, s, flags, 1,
                   static_cast<const int8_t*>(W), static_cast<const float*>(scale),
                   static_cast<const __half*>(x), static_cast<__half*>(y), N, K);
 }
 
 template <class Fmt, class Math, bool kBulk>
-cudaError_t launch_vec(const void* W, const void* scale, const void* x, void* y, int64_t N,
-                       int64_t K, cudaStream_t s, unsigned flags) {
+cudaError_t launch_vec1(const void* W, const void* scale, const void* x, void* y, int64_t N,
+                        int64_t K, cudaStream_t s, unsigned flags) {
     constexpr bool kInt4 = Fmt::kGroupScale;
     // Alignment contract of the 16-byte paths; otherwise run the scalar
     // kernel, whose output the baseline variant reproduces bit for bit.
@@ -220,83 +230,179 @@ cudaError_t launch_vec(const void* W, const void* scale, const void* x, void* y,
     const dim3 grid((unsigned)g.ctas);
     const dim3 block(kBulk ? kConsumerThreads + 32 : kConsumerThreads);
     using S = typename Fmt::Scale;
-    return launch(kernel, grid, block, (size_t)smem, s, flags, static_cast<const uint8_t*>(W),
+    return launch(kernel, grid, block, (size_t)smem, s, flags, 1, static_cast<const uint8_t*>(W),
                   static_cast<const S*>(scale), static_cast<const __half*>(x),
                   static_cast<__half*>(y), g);
 }
 
-// Geometry of the tensor-core kernels (see gemv_mma.cuh).  Returns false when
-// the staged activations do not fit in shared memory (K beyond ~100k).
-// ctas_per_sm: CTAs of one GEMV per SM before tiles are shared (1 for 8-warp
-// CTAs; 2 for 4-warp CTAs keeps the warps of one GEMV per SM unchanged).
-bool make_mma_geom(int64_t N, int64_t K, bool int4, int num_sms, int ctas_per_sm, MmaGeom& g) {
+// Kernels without a batch dimension run once per activation row.
+using Launch1 = cudaError_t (*)(const void*, const void*, const void*, void*, int64_t, int64_t,
+                                cudaStream_t, unsigned);
+template <Launch1 F>
+cudaError_t per_row(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    for (int64_t m = 0; m < a.M; ++m) {
+        cudaError_t e = F(a.W, a.scale, static_cast<const __half*>(a.x) + m * a.x_stride,
+                          static_cast<__half*>(a.y) + m * a.y_stride, a.N, a.K, s, flags);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+// ---- tensor-core kernels ----
+
+// Geometry of the tensor-core kernels (see gemv_mma.cuh).
+//   K is split (cluster of up to 8 CTAs) while the row tiles alone cannot
+//   give every SM a CTA or the staged activations of a split exceed the
+//   budget; the row groups then target SMs x ctas_per_sm CTAs (1 for 8-warp
+//   CTAs, 2 for a shorter per-launch latency), capped by max_groups (clusters
+//   that can be resident at once).  Returns false when no split fits in
+//   shared memory.
+bool make_mma_geom(int64_t N, int64_t K, int64_t M, bool int4, int num_sms, int ctas_per_sm,
+                   int64_t max_groups, MmaGeom& g) {
     g = MmaGeom{};
     g.N = N;
     g.K = K;
+    g.M = (int32_t)M;
     g.row_bytes = int4 ? K / 2 : K;
     g.blocks = (int32_t)(g.row_bytes / 64);
     g.n_kc = (g.blocks + kMmaChunkBlocks - 1) / kMmaChunkBlocks;
+    const int bw = int4 ? MmaInt4::kBlockWords : MmaInt8::kBlockWords;
+    const int pad = M > 1 ? 4 : 0;  // 64 B between activation rows: no bank conflicts
     const int64_t tiles = (N + 15) / 16;
-    int64_t ctas = std::min<int64_t>(tiles, (int64_t)num_sms * ctas_per_sm);
-    for (;;) {
-        const int64_t per = (tiles + ctas - 1) / ctas;
-        if (per * g.n_kc <= kMmaPartialMax || ctas >= tiles) break;
-        ctas = std::min<int64_t>(tiles, ctas + std::max<int64_t>(1, ctas / 8));
-    }
-    g.ctas = (int32_t)ctas;
-    g.tiles_base = (int32_t)(tiles / ctas);
-    g.tiles_rem = (int32_t)(tiles % ctas);
+    const int64_t target = (int64_t)num_sms * ctas_per_sm;
+    // Budgets keep two CTAs per SM for M <= 8 (one 16-warp CTA for M > 8).
+    const int64_t xs_budget = (M == 1 ? 96 : M <= 8 ? 80 : 144) * 1024;
+    auto xs_bytes = [&](int64_t kc_split) {
+        return M * (kc_split * kMmaChunkBlocks * bw + pad) * 16;
+    };
+    // The K split sets the summation order, so it depends on the shape and the
+    // SM count only (results do not change with the launch geometry or flags).
+    // A split is only worth its cluster reduction while every CTA keeps at
+    // least 16 items (two per warp of an 8-warp CTA).
+    int64_t S = 1;
+    while (S < kMmaMaxSplits && tiles * S < num_sms && g.n_kc >= 2 * 16 * S) S *= 2;
+    while (S < kMmaMaxSplits && xs_bytes((g.n_kc + S - 1) / S) > xs_budget && g.n_kc >= 2 * S)
+        S *= 2;
+    const int64_t kc_split = (g.n_kc + S - 1) / S;
+    S = (g.n_kc + kc_split - 1) / kc_split;  // no empty split
+    if (xs_bytes(kc_split) > xs_budget) return false;
+    g.splits = (int32_t)S;
+    g.kc_split = (int32_t)kc_split;
+    g.xs_words = (int32_t)(kc_split * kMmaChunkBlocks * bw + pad);
+    int64_t groups = std::min<int64_t>(tiles, std::max<int64_t>(1, target / S));
+    if (max_groups > 0) groups = std::min(groups, max_groups);
+    g.groups = (int32_t)groups;
+    g.tiles_base = (int32_t)(tiles / groups);
+    g.tiles_rem = (int32_t)(tiles % groups);
     const int64_t max_tiles = g.tiles_base + (g.tiles_rem > 0 ? 1 : 0);
     g.max_rows = (int32_t)std::min<int64_t>(16 * max_tiles, N);
-    g.max_items = (int32_t)(max_tiles * g.n_kc);
-    if (g.max_items > kMmaPartialMax) return false;
-    g.xs_bytes = (int32_t)(K * 2);
+    const int64_t part_budget = (M == 1 ? 32 : M <= 8 ? 24 : 48) * 1024;
+    const int64_t per_tile = kc_split * 16 * M * 4;
+    const int64_t rt = std::max<int64_t>(1, std::min<int64_t>(max_tiles, part_budget / per_tile));
+    g.round_tiles = (int32_t)rt;
+    g.part_floats = (int32_t)(rt * kc_split * 16 * M);
     return mma_smem_total(g) <= 226 * 1024;  // 1 KiB left for static shared memory
 }
 
+// Clusters of one kernel / size / shared-memory footprint that can be
+// resident at once (cached: the query costs a driver call per launch).
+template <class K>
+cudaError_t max_active_clusters(K kernel, const cudaLaunchConfig_t& cfg, int dev, int& out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, unsigned, size_t, unsigned>, int> cache;
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), dev,
+                                     cfg.attrs[0].val.clusterDim.x, cfg.dynamicSmemBytes,
+                                     cfg.blockDim.x);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return cudaSuccess;
+    }
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&out, kernel, &cfg);
+    if (e == cudaSuccess) cache[key] = out;
+    return e;
+}
+
+// Launch of one tensor-core GEMV (kNB from M).  Peer mode: rows go to every
+// rank's buffers (`po`); the sharded entry points check the contract first.
 template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer>
-cudaError_t launch_mma_impl(const void* W, const void* scale, const void* x, void* y, int64_t N,
-                            int64_t K, cudaStream_t s, unsigned flags, const PeerOut& po) {
+cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, const PeerOut& po) {
     constexpr bool kInt4 = Fmt::kGroupScale;
-    const bool ok = aligned16(W) && aligned16(x) && (kInt4 ? (K % 128 == 0) : (K % 64 == 0));
+    const bool ok = aligned16(a.W) && aligned16(a.x) && (a.x_stride % 8) == 0 &&
+                    (kInt4 ? (a.K % 128 == 0) : (a.K % 64 == 0)) && a.M >= 1 &&
+                    a.M <= kMmaMaxM;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     MmaGeom g;
-    if constexpr (kPeer) {
-        // the sharded entry points check this contract before launching
-        if (!ok) return cudaErrorMisalignedAddress;
-        if (!make_mma_geom(N, K, kInt4, sm_count(dev), kCtasPerSm, g))
-            return cudaErrorInvalidConfiguration;
-    } else if (!ok || !make_mma_geom(N, K, kInt4, sm_count(dev), kCtasPerSm, g)) {
-        return kInt4 ? launch_int4_scalar(W, scale, x, y, N, K, s, flags)
-                     : launch_int8_scalar(W, scale, x, y, N, K, s, flags);
+    const bool geom = ok && make_mma_geom(a.N, a.K, a.M, kInt4, sm_count(dev), kCtasPerSm, 0, g);
+    if (!geom) {
+        if constexpr (kPeer) return ok ? cudaErrorInvalidConfiguration : cudaErrorMisalignedAddress;
+        return per_row<kInt4 ? launch_int4_scalar : launch_int8_scalar>(a, s, flags);
     }
+    g.x_stride = a.x_stride;
+    g.y_stride = a.y_stride;
     g.early_x = (flags & 3u) == 3u ? 1 : 0;
-    const int smem = mma_smem_total(g);
     const bool all_full = (g.blocks % kMmaChunkBlocks) == 0;
-    auto kernel = all_full ? gemv_mma_kernel<Fmt, kWarps, true, kPeer>
-                           : gemv_mma_kernel<Fmt, kWarps, false, kPeer>;
-    if (smem > 48 * 1024) {
-        e = ensure_smem_attr(kernel, dev, smem);
-        if (e != cudaSuccess) return e;
-    }
     using S = typename Fmt::Scale;
-    return launch(kernel, dim3((unsigned)g.ctas), dim3(32 * kWarps), (size_t)smem, s, flags,
-                  static_cast<const uint8_t*>(W), static_cast<const S*>(scale),
-                  static_cast<const __half*>(x), static_cast<__half*>(y), g, po);
+    auto go = [&](auto kernel) -> cudaError_t {
+        int smem = mma_smem_total(g);
+        cudaError_t err = ensure_smem_attr(kernel, dev, smem);
+        if (err != cudaSuccess) return err;
+        if (g.splits > 1) {
+            // keep every cluster of the launch resident at once
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3((unsigned)(g.groups * g.splits));
+            cfg.blockDim = dim3(32 * kWarps);
+            cfg.dynamicSmemBytes = (size_t)smem;
+            cudaLaunchAttribute at;
+            at.id = cudaLaunchAttributeClusterDimension;
+            at.val.clusterDim.x = (unsigned)g.splits;
+            at.val.clusterDim.y = 1;
+            at.val.clusterDim.z = 1;
+            cfg.attrs = &at;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            err = max_active_clusters(kernel, cfg, dev, clusters);
+            if (err != cudaSuccess) return err;
+            if (clusters <= 0) return cudaErrorInvalidConfiguration;
+            if (clusters < g.groups) {
+                const int64_t x_stride = g.x_stride, y_stride = g.y_stride;
+                const int early = g.early_x;
+                if (!make_mma_geom(a.N, a.K, a.M, kInt4, sm_count(dev), kCtasPerSm, clusters, g))
+                    return cudaErrorInvalidConfiguration;
+                g.x_stride = x_stride;
+                g.y_stride = y_stride;
+                g.early_x = early;
+                smem = mma_smem_total(g);
+                if ((err = ensure_smem_attr(kernel, dev, smem)) != cudaSuccess) return err;
+            }
+        }
+        return launch(kernel, dim3((unsigned)(g.groups * g.splits)), dim3(32 * kWarps),
+                      (size_t)smem, s, flags, g.splits, static_cast<const uint8_t*>(a.W),
+                      static_cast<const S*>(a.scale), static_cast<const __half*>(a.x),
+                      static_cast<__half*>(a.y), g, po);
+    };
+    if (a.M == 1) {
+        return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 0, true, kPeer>)
+                        : go(gemv_mma_kernel<Fmt, kWarps, 0, false, kPeer>);
+    }
+    if (a.M <= 8) {
+        return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 1, true, kPeer>)
+                        : go(gemv_mma_kernel<Fmt, kWarps, 1, false, kPeer>);
+    }
+    return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 2, true, kPeer>)
+                    : go(gemv_mma_kernel<Fmt, kWarps, 2, false, kPeer>);
 }
 
 template <class Fmt, int kWarps, int kCtasPerSm>
-cudaError_t launch_mma(const void* W, const void* scale, const void* x, void* y, int64_t N,
-                       int64_t K, cudaStream_t s, unsigned flags) {
-    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, false>(W, scale, x, y, N, K, s, flags,
-                                                           PeerOut{});
+cudaError_t launch_mma(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, false>(a, s, flags, PeerOut{});
 }
 
 template <class Fmt, int kWarps, int kCtasPerSm>
-cudaError_t launch_mma_sharded(const void* W, const void* scale, const void* x,
-                               const PeerArgs& pa, int64_t N_shard, int64_t K, cudaStream_t s,
+cudaError_t launch_mma_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
                                unsigned flags) {
     if (pa.world < 1 || pa.world > kMaxPeers || pa.rank < 0 || pa.rank >= pa.world)
         return cudaErrorInvalidValue;
@@ -309,8 +415,7 @@ cudaError_t launch_mma_sharded(const void* W, const void* scale, const void* x,
     po.row0 = pa.row0;
     po.rank = pa.rank;
     po.world = pa.world;
-    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, true>(W, scale, x, nullptr, N_shard, K, s,
-                                                          flags, po);
+    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, true>(a, s, flags, po);
 }
 
 // Geometry chosen per call (measured on B200 with L2-cold pools):
@@ -318,34 +423,41 @@ cudaError_t launch_mma_sharded(const void* W, const void* scale, const void* x,
 //    one per SM per GEMV, so up to four GEMVs overlap on an SM; 8-warp CTAs
 //    once K > 16384 (the staged activations then limit co-residency);
 //  * chained or plain launches: 8-warp CTAs, two per SM per GEMV (shorter
-//    per-GEMV latency), one per SM for K <= 2048.
+//    per-GEMV latency), one per SM for K <= 2048;
+//  * 2..8 activation rows: 8-warp CTAs (two fit on an SM), one per SM per
+//    launch for independent launches, two for chained ones;
+//  * 9..16 rows: one 16-warp CTA per SM (two column blocks need the registers).
 template <class Fmt>
-cudaError_t launch_mma_auto(const void* W, const void* scale, const void* x, void* y, int64_t N,
-                            int64_t K, cudaStream_t s, unsigned flags) {
+cudaError_t launch_mma_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    if (a.M > 8) return launch_mma<Fmt, 16, 1>(a, s, flags);
+    if (a.M > 1)
+        return (flags & 3u) == 3u ? launch_mma<Fmt, 8, 1>(a, s, flags)
+                                  : launch_mma<Fmt, 8, 2>(a, s, flags);
     if ((flags & 3u) == 3u)
-        return K <= 16384 ? launch_mma<Fmt, 4, 1>(W, scale, x, y, N, K, s, flags)
-                          : launch_mma<Fmt, 8, 1>(W, scale, x, y, N, K, s, flags);
-    return K <= 2048 ? launch_mma<Fmt, 8, 1>(W, scale, x, y, N, K, s, flags)
-                     : launch_mma<Fmt, 8, 2>(W, scale, x, y, N, K, s, flags);
+        return a.K <= 16384 ? launch_mma<Fmt, 4, 1>(a, s, flags) : launch_mma<Fmt, 8, 1>(a, s, flags);
+    return a.K <= 2048 ? launch_mma<Fmt, 8, 1>(a, s, flags) : launch_mma<Fmt, 8, 2>(a, s, flags);
 }
 
 template <class Fmt>
-cudaError_t launch_mma_sharded_auto(const void* W, const void* scale, const void* x,
-                                    const PeerArgs& pa, int64_t N, int64_t K, cudaStream_t s,
+cudaError_t launch_mma_sharded_auto(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
                                     unsigned flags) {
+    if (a.M > 8) return launch_mma_sharded<Fmt, 16, 1>(a, pa, s, flags);
+    if (a.M > 1)
+        return (flags & 3u) == 3u ? launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags)
+                                  : launch_mma_sharded<Fmt, 8, 2>(a, pa, s, flags);
     if ((flags & 3u) == 3u)
-        return K <= 16384 ? launch_mma_sharded<Fmt, 4, 1>(W, scale, x, pa, N, K, s, flags)
-                          : launch_mma_sharded<Fmt, 8, 1>(W, scale, x, pa, N, K, s, flags);
-    return K <= 2048 ? launch_mma_sharded<Fmt, 8, 1>(W, scale, x, pa, N, K, s, flags)
-                     : launch_mma_sharded<Fmt, 8, 2>(W, scale, x, pa, N, K, s, flags);
+        return a.K <= 16384 ? launch_mma_sharded<Fmt, 4, 1>(a, pa, s, flags)
+                            : launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags);
+    return a.K <= 2048 ? launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags)
+                       : launch_mma_sharded<Fmt, 8, 2>(a, pa, s, flags);
 }
 
 const VariantDesc kInt4Variants[] = {
-    {"int4gemv_baseline", launch_int4_scalar, false},
-    {"int4gemv_bulk", launch_vec<Int4Fmt, MathF16, true>, false},
-    {"int4gemv_bulk_f32x2", launch_vec<Int4Fmt, MathF32x2, true>, false},
-    {"int4gemv_ldg", launch_vec<Int4Fmt, MathF16, false>, false},
-    {"int4gemv_ldg_f32x2", launch_vec<Int4Fmt, MathF32x2, false>, false},
+    {"int4gemv_baseline", per_row<launch_int4_scalar>, false},
+    {"int4gemv_bulk", per_row<launch_vec1<Int4Fmt, MathF16, true>>, false},
+    {"int4gemv_bulk_f32x2", per_row<launch_vec1<Int4Fmt, MathF32x2, true>>, false},
+    {"int4gemv_ldg", per_row<launch_vec1<Int4Fmt, MathF16, false>>, false},
+    {"int4gemv_ldg_f32x2", per_row<launch_vec1<Int4Fmt, MathF32x2, false>>, false},
     {"int4gemv_mma", launch_mma_auto<MmaInt4>, false},
     {"int4gemv_mma_w4", launch_mma<MmaInt4, 4, 1>, false},
     {"int4gemv_mma_w8", launch_mma<MmaInt4, 8, 1>, false},
@@ -354,11 +466,11 @@ const VariantDesc kInt4Variants[] = {
 };
 
 const VariantDesc kInt8Variants[] = {
-    {"qgemv_baseline", launch_int8_scalar, false},
-    {"qgemv_bulk", launch_vec<Int8Fmt, MathF16, true>, false},
-    {"qgemv_bulk_f32x2", launch_vec<Int8Fmt, MathF32x2, true>, false},
-    {"qgemv_ldg", launch_vec<Int8Fmt, MathF16, false>, false},
-    {"qgemv_ldg_f32x2", launch_vec<Int8Fmt, MathF32x2, false>, false},
+    {"qgemv_baseline", per_row<launch_int8_scalar>, false},
+    {"qgemv_bulk", per_row<launch_vec1<Int8Fmt, MathF16, true>>, false},
+    {"qgemv_bulk_f32x2", per_row<launch_vec1<Int8Fmt, MathF32x2, true>>, false},
+    {"qgemv_ldg", per_row<launch_vec1<Int8Fmt, MathF16, false>>, false},
+    {"qgemv_ldg_f32x2", per_row<launch_vec1<Int8Fmt, MathF32x2, false>>, false},
     {"qgemv_mma", launch_mma_auto<MmaInt8>, false},
     {"qgemv_mma_w4", launch_mma<MmaInt8, 4, 1>, false},
     {"qgemv_mma_w8", launch_mma<MmaInt8, 8, 1>, false},

@@ -8,11 +8,21 @@
 
 namespace clb {
 
-// Launches one GEMV of a given variant.  W is uint8 (INT4 packed) or int8
-// (INT8); scale is fp16 [N, K/128] (INT4) or fp32 [N] (INT8).  flags are the
-// CL_LAUNCH_* bits of the public header.
-using LaunchFn = cudaError_t (*)(const void* W, const void* scale, const void* x, void* y,
-                                 int64_t N, int64_t K, cudaStream_t stream, unsigned flags);
+// One launch: W is uint8 [N, K/2] (INT4 packed) or int8 [N, K] (INT8); scale
+// is fp16 [N, K/128] (INT4) or fp32 [N] (INT8); x holds M activation rows of
+// K halves (x_stride halves apart), y receives M rows of N halves (y_stride
+// apart; in peer mode, rows of the full matrix in every rank's buffer).
+struct GemvArgs {
+    const void* W;
+    const void* scale;
+    const void* x;
+    void* y;
+    int64_t N, K, M;
+    int64_t x_stride, y_stride;
+};
+
+// flags are the CL_LAUNCH_* bits of the public header.
+using LaunchFn = cudaError_t (*)(const GemvArgs& args, cudaStream_t stream, unsigned flags);
 
 struct VariantDesc {
     const char* name;
@@ -30,8 +40,7 @@ struct PeerArgs {
     int rank, world;
 };
 
-using ShardedLaunchFn = cudaError_t (*)(const void* W, const void* scale, const void* x,
-                                        const PeerArgs& peers, int64_t N_shard, int64_t K,
+using ShardedLaunchFn = cudaError_t (*)(const GemvArgs& args, const PeerArgs& peers,
                                         cudaStream_t stream, unsigned flags);
 
 struct ShardedVariantDesc {

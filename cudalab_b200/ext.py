@@ -118,6 +118,47 @@ class _ExtBase:
         self._validate_out(W, out)
         self._launch(variant, W, scale, x, out, flags)
 
+    # ---- batched activations (no reference counterpart; English messages) ----
+    def _validate_batch(self, W, X: torch.Tensor, K: int) -> int:
+        _chk(X.dim() == 2, f"X must be 2-D (M, K), got {X.dim()}-D")
+        _chk(X.size(0) > 0, "X must have at least one row")
+        _chk(X.size(1) == K, f"X must have K={K} columns, got {X.size(1)}")
+        _chk(X.dtype == torch.float16, f"X must be float16, got {X.dtype}")
+        _chk(X.is_contiguous(), "X must be contiguous")
+        _chk(X.is_cuda and X.device == W.device, f"X must be on the device of {self.w_name}")
+        return X.size(0)
+
+    def _launch_batched(self, name: str, W, scale, X, out, flags: int) -> None:
+        N, K, M = W.size(0), self._k_of(W), X.size(0)
+        dev = W.device
+        with torch.cuda.device(dev):
+            rc = self._batched(name.encode(), W.data_ptr(), scale.data_ptr(), X.data_ptr(),
+                               out.data_ptr(), M, N, K, _stream_ptr(dev), flags)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"{self.kind} batched launch failed ({rc}): "
+                               f"{nat.last_error(self._lib)}")
+
+    def forward_batched(self, variant: str, W, scale, X, flags: int = 0) -> torch.Tensor:
+        """Y [M, N] = rows of X [M, K] through the quantised W."""
+        self._check_variant(variant)
+        self._validate_w(W)
+        self._validate_scale(W, scale)
+        M = self._validate_batch(W, X, self._k_of(W))
+        out = torch.empty(M, W.size(0), dtype=torch.float16, device=W.device)
+        self._launch_batched(variant, W, scale, X, out, flags)
+        return out
+
+    def forward_batched_into(self, variant: str, W, scale, X, out, flags: int = 0) -> None:
+        self._check_variant(variant)
+        self._validate_w(W)
+        self._validate_scale(W, scale)
+        M = self._validate_batch(W, X, self._k_of(W))
+        _chk(out.dim() == 2 and out.size(0) == M and out.size(1) == W.size(0),
+             f"out must be [M={M}, N={W.size(0)}]")
+        _chk(out.dtype == torch.float16 and out.is_contiguous(), "out must be contiguous float16")
+        _chk(out.is_cuda and out.device == W.device, f"out must be on the device of {self.w_name}")
+        self._launch_batched(variant, W, scale, X, out, flags)
+
     def native_timing(self, variant: str, W, scale, x, out, warmup: int = 200,
                       n_windows: int = 10, launches_per_window: int = 64,
                       flags: int = 0) -> dict:
@@ -162,6 +203,7 @@ class Int4gemvExt(_ExtBase):
     def __init__(self) -> None:
         super().__init__()
         self._call = self._lib.cl_int4gemv_ex
+        self._batched = self._lib.cl_int4gemv_batched
         self._timing = self._lib.cl_int4gemv_native_timing
 
     def _k_of(self, W) -> int:
@@ -207,6 +249,7 @@ class QgemvExt(_ExtBase):
     def __init__(self) -> None:
         super().__init__()
         self._call = self._lib.cl_qgemv_ex
+        self._batched = self._lib.cl_qgemv_batched
         self._timing = self._lib.cl_qgemv_native_timing
 
     def _k_of(self, W) -> int:

@@ -42,16 +42,23 @@ def shard_rows(N: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def gather_shards(y_shard: torch.Tensor, y_gather: torch.Tensor, N: int, group=None) -> torch.Tensor:
-    """All-gather of equally padded shards (`y_shard` holds n_max = ceil(N/world)
-    values, the first shard_rows(...)[1] of them valid) into y [N]: a view of
-    `y_gather` when N divides evenly, else a packed copy."""
+    """All-gather of equally padded shards into y.  `y_shard` is [n_max] or
+    [M, n_max] (n_max = ceil(N/world), the first shard_rows(...)[1] columns
+    valid); `y_gather` holds world * M * n_max values.  Returns y [N] (a view
+    of `y_gather` when N divides evenly) or [M, N]."""
     world = dist.get_world_size(group)
-    n_max = y_shard.shape[0]
-    dist.all_gather_into_tensor(y_gather, y_shard, group=group)
-    if N == world * n_max:
-        return y_gather
-    parts = [y_gather[p * n_max: p * n_max + shard_rows(N, world, p)[1]] for p in range(world)]
-    return torch.cat(parts)
+    n_max = y_shard.shape[-1]
+    dist.all_gather_into_tensor(y_gather, y_shard.reshape(-1), group=group)
+    if y_shard.dim() == 1:
+        if N == world * n_max:
+            return y_gather
+        parts = [y_gather[p * n_max: p * n_max + shard_rows(N, world, p)[1]]
+                 for p in range(world)]
+        return torch.cat(parts)
+    M = y_shard.shape[0]
+    g = y_gather.view(world, M, n_max)
+    parts = [g[p, :, : shard_rows(N, world, p)[1]] for p in range(world)]
+    return torch.cat(parts, dim=1)
 
 
 def _round_up(v: int, a: int = _ALIGN) -> int:
@@ -60,12 +67,14 @@ def _round_up(v: int, a: int = _ALIGN) -> int:
 
 @dataclass
 class _Layout:
-    """One rank's peer allocation: [y parity 0 | y parity 1 | flag block]."""
+    """One rank's peer allocation: [y parity 0 | y parity 1 | flag block]; a y
+    buffer holds up to max_batch rows of N halves."""
     N: int
+    max_batch: int = 1
 
     @property
     def y_bytes(self) -> int:
-        return _round_up(2 * self.N)
+        return _round_up(2 * self.N * self.max_batch)
 
     def y_off(self, parity: int) -> int:
         return parity * self.y_bytes
@@ -121,13 +130,15 @@ class PeerBuffers:
     all_gather_object over `group`; `backend` supplies alloc/open/close/free
     (the C ABI by default)."""
 
-    def __init__(self, N_total: int, group=None, backend=None):
+    def __init__(self, N_total: int, group=None, backend=None, max_batch: int = 1):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         if self.world > nat.CL_MAX_PEERS:
             raise ValueError(f"at most {nat.CL_MAX_PEERS} ranks, got {self.world}")
-        self.layout = _Layout(N_total)
+        if not 1 <= max_batch <= 16:
+            raise ValueError(f"max_batch must be in [1, 16], got {max_batch}")
+        self.layout = _Layout(N_total, max_batch)
         self.backend = backend or _CudaBackend()
         self.local_ptr, handle = self.backend.alloc(self.layout.total)
         handles = [None] * self.world
@@ -155,8 +166,10 @@ class PeerBuffers:
         return self._flag_array
 
     def local_y(self, parity: int) -> torch.Tensor:
+        """This rank's y buffer of one parity as a flat [max_batch * N] view."""
         ptr = self.local_ptr + self.layout.y_off(parity)
-        return torch.as_tensor(_DeviceView(ptr, self.layout.N, "<f2"), device="cuda")
+        n = self.layout.N * self.layout.max_batch
+        return torch.as_tensor(_DeviceView(ptr, n, "<f2"), device="cuda")
 
     def close(self) -> None:
         for ptr in self._opened:
@@ -172,7 +185,8 @@ class ShardedGemv:
 
     kind: "int4gemv" (W_shard uint8 [n, K/2], scale fp16 [n, K/128]) or
     "qgemv" (W_shard int8 [n, K], scale fp32 [n]); the shard holds rows
-    shard_rows(N_total, world, rank).  forward(x) returns y [N_total] fp16 on
+    shard_rows(N_total, world, rank).  forward(x) takes x [K] or X [M, K]
+    (M <= max_batch <= 16) and returns y [N_total] or Y [M, N_total] fp16 on
     every rank.  In fused mode the returned tensor is this step's parity
     buffer: it stays valid until the step after next (two steps later the
     same buffer is rewritten).  Every rank must call forward the same number
@@ -183,7 +197,8 @@ class ShardedGemv:
 
     def __init__(self, kind: str, W_shard: torch.Tensor, scale_shard: torch.Tensor,
                  N_total: int, K: int, group=None, variant: str | None = None,
-                 mode: str = "fused", backend=None, peers: "PeerBuffers | None" = None):
+                 mode: str = "fused", backend=None, peers: "PeerBuffers | None" = None,
+                 max_batch: int = 1):
         if kind not in ("int4gemv", "qgemv"):
             raise ValueError(f"unknown kind {kind}")
         if mode not in ("fused", "nccl"):
@@ -198,14 +213,16 @@ class ShardedGemv:
                              f"expected {self.n} (rows {self.row0}..{self.row0 + self.n})")
         self.W, self.scale = W_shard.contiguous(), scale_shard.contiguous()
         self.variant = variant or ("int4gemv_mma" if kind == "int4gemv" else "qgemv_mma")
+        self.max_batch = max_batch
         self.epoch = 0
         if mode == "fused":
             self.lib = nat.load()
             # several weight sets of one shape may share the buffers (and the step count)
             self._own_peers = peers is None
-            self.peers = peers if peers is not None else PeerBuffers(N_total, group, backend)
-            if self.peers.layout.N != N_total:
-                raise ValueError("shared peer buffers were made for another N")
+            self.peers = (peers if peers is not None
+                          else PeerBuffers(N_total, group, backend, max_batch))
+            if self.peers.layout.N != N_total or self.peers.layout.max_batch < max_batch:
+                raise ValueError("shared peer buffers were made for another N or batch")
             self._fn = (self.lib.cl_int4gemv_sharded if kind == "int4gemv"
                         else self.lib.cl_qgemv_sharded)
             self._y = [self.peers.local_y(0), self.peers.local_y(1)]
@@ -214,24 +231,38 @@ class ShardedGemv:
             self.ext = build(kind)
             self.n_max = -(-N_total // self.world)
             dev = self.W.device
-            self.y_shard = torch.empty(self.n_max, dtype=torch.float16, device=dev)
-            self.y_gather = torch.empty(self.world * self.n_max, dtype=torch.float16, device=dev)
+            self.y_shard = torch.zeros(max_batch, self.n_max, dtype=torch.float16, device=dev)
+            self.y_gather = torch.empty(self.world * max_batch * self.n_max, dtype=torch.float16,
+                                        device=dev)
 
     def forward(self, x: torch.Tensor, flags: int = 0) -> torch.Tensor:
-        if x.dtype != torch.float16 or x.dim() != 1 or x.shape[0] != self.K:
-            raise RuntimeError(f"x must be fp16 [{self.K}]")
+        if x.dtype != torch.float16 or x.dim() not in (1, 2) or x.shape[-1] != self.K:
+            raise RuntimeError(f"x must be fp16 [{self.K}] or [M, {self.K}]")
+        M = 1 if x.dim() == 1 else x.shape[0]
+        if not 1 <= M <= self.max_batch:
+            raise RuntimeError(f"batch of {M} rows exceeds max_batch={self.max_batch}")
+        x = x.contiguous()
         self.epoch += 1
         if self.mode == "nccl":
-            self.ext.forward_into(self.variant, self.W, self.scale, x, self.y_shard[: self.n],
-                                  flags=flags)
-            return gather_shards(self.y_shard, self.y_gather, self.N, self.group)
+            if x.dim() == 1:
+                self.ext.forward_into(self.variant, self.W, self.scale, x,
+                                      self.y_shard[0, : self.n], flags=flags)
+                g = self.y_gather[: self.world * self.n_max]
+                return gather_shards(self.y_shard[0], g, self.N, self.group)
+            ys = self.y_shard[:M]
+            out = torch.empty(M, self.n, dtype=torch.float16, device=x.device)
+            self.ext.forward_batched_into(self.variant, self.W, self.scale, x, out, flags=flags)
+            ys[:, : self.n].copy_(out)
+            g = self.y_gather[: self.world * M * self.n_max]
+            return gather_shards(ys, g, self.N, self.group)
         stream = torch.cuda.current_stream(self.W.device).cuda_stream
         rc = self._fn(self.variant.encode(), self.W.data_ptr(), self.scale.data_ptr(),
-                      x.data_ptr(), self.peers.y_array(), self.peers.flag_array(),
+                      x.data_ptr(), M, self.peers.y_array(), self.peers.flag_array(),
                       self.rank, self.world, self.row0, self.n, self.N, self.K, stream, flags)
         if rc != nat.CL_OK:
             raise RuntimeError(f"{self.kind} sharded step failed ({rc}): {nat.last_error()}")
-        return self._y[self.epoch & 1]
+        y = self._y[self.epoch & 1]
+        return y[: self.N] if x.dim() == 1 else y[: M * self.N].view(M, self.N)
 
     def close(self) -> None:
         if self.mode == "fused" and self._own_peers:

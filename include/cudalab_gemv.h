@@ -83,6 +83,16 @@ int cl_int4gemv(const char* variant, const uint8_t* W_packed, const void* scale,
 int cl_int4gemv_ex(const char* variant, const uint8_t* W_packed, const void* scale,
                    const void* x, void* out, int64_t N, int64_t K, void* stream, uint32_t flags);
 
+/* Batched form (no reference counterpart: the reference's operator is M = 1;
+ * its sharded 70B-class configuration uses M in {1, 4, 16}): X fp16 [M, K] ->
+ * Y fp16 [M, N], both row-major and contiguous, M >= 1.  The tensor-core
+ * variants dequantise each weight once per 16 activation rows; the other
+ * variants run once per row.  Row m of Y equals cl_int4gemv_ex on row m of X
+ * up to the fp32 summation order of the variant. */
+int cl_int4gemv_batched(const char* variant, const uint8_t* W_packed, const void* scale,
+                        const void* X, void* Y, int64_t M, int64_t N, int64_t K, void* stream,
+                        uint32_t flags);
+
 /* Replaces `native_timing` of kernels/int4gemv/bindings.cpp:180-253: `warmup`
  * untimed launches, then `n_windows` windows of `launches_per_window`
  * back-to-back launches bracketed by CUDA events on `stream`; writes the
@@ -107,6 +117,10 @@ int cl_qgemv(const char* variant, const int8_t* W_q, const float* scale, const v
 
 int cl_qgemv_ex(const char* variant, const int8_t* W_q, const float* scale, const void* x,
                 void* out, int64_t N, int64_t K, void* stream, uint32_t flags);
+
+/* Batched INT8 (same contract as cl_int4gemv_batched). */
+int cl_qgemv_batched(const char* variant, const int8_t* W_q, const float* scale, const void* X,
+                     void* Y, int64_t M, int64_t N, int64_t K, void* stream, uint32_t flags);
 
 /* Replaces `native_timing` of kernels/qgemv/bindings.cpp (same contract as
  * cl_int4gemv_native_timing). */
@@ -144,8 +158,9 @@ int cl_peer_free(void* ptr);
 
 /* One step of the sharded INT4 GEMV on this rank.
  *   W_shard [N_shard, K/2], scale_shard [N_shard, K/128]: rows
- *     [row0, row0 + N_shard) of the full matrix; x [K] (same on every rank).
- *   y_peers[2 * world]: every rank's two y buffers (N_total halves each) as
+ *     [row0, row0 + N_shard) of the full matrix; x fp16 [M, K], 1 <= M <= 16
+ *     (the same on every rank).
+ *   y_peers[2 * world]: every rank's two y buffers ([M, N_total] halves) as
  *     pointers valid in this process, parity-0 buffers of ranks 0..world-1
  *     first, then the parity-1 buffers (own rank: local pointers).
  *   flag_peers[world]: every rank's flag block (CL_PEER_FLAG_BYTES, zero
@@ -156,14 +171,14 @@ int cl_peer_free(void* ptr);
  * seconds for another records status 5 (cl_device_status) instead of
  * hanging; the group must then be set up again. */
 int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void* scale_shard,
-                        const void* x, void* const* y_peers, void* const* flag_peers, int rank,
-                        int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
-                        void* stream, uint32_t flags);
+                        const void* x, int64_t M, void* const* y_peers, void* const* flag_peers,
+                        int rank, int world, int64_t row0, int64_t N_shard, int64_t N_total,
+                        int64_t K, void* stream, uint32_t flags);
 /* Same for INT8 (W_shard int8 [N_shard, K], scale_shard fp32 [N_shard], K % 64 == 0). */
 int cl_qgemv_sharded(const char* variant, const int8_t* W_shard, const float* scale_shard,
-                     const void* x, void* const* y_peers, void* const* flag_peers, int rank,
-                     int world, int64_t row0, int64_t N_shard, int64_t N_total, int64_t K,
-                     void* stream, uint32_t flags);
+                     const void* x, int64_t M, void* const* y_peers, void* const* flag_peers,
+                     int rank, int world, int64_t row0, int64_t N_shard, int64_t N_total,
+                     int64_t K, void* stream, uint32_t flags);
 
 #ifdef __cplusplus
 } /* extern "C" */
