@@ -510,25 +510,48 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     // kernel, x may only be read after that kernel has completed.
     if (!g.early_x) pdl_wait_prior_grids();
     // Activations of this split: INT4 in the permuted step order, INT8 as is.
+    // (row m, word q) pairs are walked in order, kStageBatch loads in flight
+    // per thread before their stores.
     {
+        constexpr int kStageBatch = 4;
         const int words = lblocks * Fmt::kBlockWords;
         const int64_t k_first = (int64_t)kMmaChunkBlocks * kc0 * Fmt::kBlockWords * 8;
-        for (int m = 0; m < M; ++m) {
-            const uint4* src = reinterpret_cast<const uint4*>(x + m * g.x_stride + k_first);
-            uint4* row = xs4 + m * g.xs_words;
-            for (int q = tid; q < words; q += kThreads) {
-                const uint4 v = __ldg(src + q);
+        int m = 0, q = tid;
+        while (m < M && q >= words) {
+            q -= words;
+            ++m;
+        }
+        while (m < M) {
+            uint4 v[kStageBatch];
+            int qs[kStageBatch], ms[kStageBatch];
+#pragma unroll
+            for (int u = 0; u < kStageBatch; ++u) {
+                ms[u] = m;
+                qs[u] = q;
+                if (m < M)
+                    v[u] = __ldg(reinterpret_cast<const uint4*>(x + m * g.x_stride + k_first) + q);
+                q += kThreads;
+                while (m < M && q >= words) {
+                    q -= words;
+                    ++m;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kStageBatch; ++u) {
+                if (ms[u] >= M) break;
+                uint4* row = xs4 + ms[u] * g.xs_words;
                 if constexpr (Fmt::kGroupScale) {
-                    const int blk = q >> 4, tt = (q >> 2) & 3, w = q & 3;
+                    const int qq = qs[u];
+                    const int blk = qq >> 4, tt = (qq >> 2) & 3, w = qq & 3;
                     // entry (blk, w, tt): step 2w (x0, x4, x1, x5), step 2w+1 (x2, x6, x3, x7)
                     uint4 e;
-                    e.x = prmt_i<0x5410u>(v.x, v.z);
-                    e.y = prmt_i<0x7632u>(v.x, v.z);
-                    e.z = prmt_i<0x5410u>(v.y, v.w);
-                    e.w = prmt_i<0x7632u>(v.y, v.w);
+                    e.x = prmt_i<0x5410u>(v[u].x, v[u].z);
+                    e.y = prmt_i<0x7632u>(v[u].x, v[u].z);
+                    e.z = prmt_i<0x5410u>(v[u].y, v[u].w);
+                    e.w = prmt_i<0x7632u>(v[u].y, v[u].w);
                     row[(blk * 4 + w) * 4 + tt] = e;
                 } else {
-                    row[q] = v;
+                    row[qs[u]] = v[u];
                 }
             }
         }

@@ -71,12 +71,14 @@ ROOT = Path(__file__).resolve().parents[2]
 
 def driver_main(argv=None) -> int:
     """The profiled program: builds a small L2-cold pool and launches each
-    weight set once (ncu flushes caches before every replay pass anyway)."""
+    weight set once (ncu flushes caches before every replay pass anyway).
+    --M > 1 launches the batched entry point with M activation rows."""
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="int4gemv")
     ap.add_argument("--variant", default="int4gemv_bulk")
     ap.add_argument("--N", type=int, default=4096)
     ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--M", type=int, default=1)
     ap.add_argument("--pool", type=int, default=4)
     ap.add_argument("--launches", type=int, default=6)
     ap.add_argument("--pdl", type=int, default=0)
@@ -88,10 +90,18 @@ def driver_main(argv=None) -> int:
     op = get(a.op)
     ext = build(a.op)
     pool = op.make_bench_pool(a.N, a.K, mode="l2cold", pool_size=a.pool, weight_dist=0.02)
-    for i in range(a.launches):
-        pool.launch(ext, a.variant, i, flags=a.pdl)
+    if a.M == 1:
+        for i in range(a.launches):
+            pool.launch(ext, a.variant, i, flags=a.pdl)
+    else:
+        X = torch.randn(a.M, a.K, device="cuda").half()
+        Y = torch.empty(a.M, a.N, device="cuda", dtype=torch.float16)
+        weights = pool.shared["weights"]
+        for i in range(a.launches):
+            W, s = weights[i % len(weights)]
+            ext.forward_batched_into(a.variant, W, s, X, Y, flags=a.pdl)
     torch.cuda.synchronize()
-    print("profile driver done", a.variant, a.N, a.K)
+    print("profile driver done", a.variant, a.N, a.K, a.M)
     return 0
 
 
