@@ -6,13 +6,15 @@ Workload (BASELINE metric "W4A16 GEMV us & HBM GB/s at 4096x4096, streaming"):
   a pool of 64 independently seeded weight sets (64 x 8.67 MB = 555 MB, far
   above the 126 MB L2) and 64 x / y buffers, cycled launch by launch, so every
   launch streams its weights from HBM.  One step = one pass over the pool (64
-  GEMVs), captured once in a CUDA graph and replayed.  Consecutive GEMVs use
-  programmatic dependent launch; in the streaming regime the activations of a
-  GEMV are not produced by the GEMV before it (CL_LAUNCH_INPUTS_READY), so a
-  GEMV streams its weights and computes while the previous one finishes and
-  only its store of y waits.  The same pool is also timed as a fully
-  dependent chain (CL_LAUNCH_PDL: x read after the previous kernel completes)
-  and with plain stream order, and the INT8 sibling on the same harness.
+  GEMVs), captured once in a CUDA graph and replayed.  The pool's GEMVs are
+  independent (their x, W and y are distinct buffers, as in the reference's
+  streaming bench), so the headline mode launches them with programmatic
+  dependent launch and declares both facts (CL_LAUNCH_PDL |
+  CL_LAUNCH_INPUTS_READY | CL_LAUNCH_OUTPUTS_FREE): a GEMV streams its
+  weights, computes and stores while earlier ones finish, and one CTA per GEMV
+  keeps the completion order.  The same pool is also timed with x read after
+  the previous GEMV (inputs-ready only: y stores wait), as a fully dependent
+  chain (CL_LAUNCH_PDL) and in plain stream order, plus the INT8 sibling.
 
 value   = algorithmic bytes moved by all ranks / max-over-ranks device time
           (GB/s; bytes per GEMV = N*K/2 + N*K/64 + 2K + 2N = 8,667,136).
@@ -214,7 +216,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--variant", default="int4gemv_mma")
     ap.add_argument("--int8-variant", default="qgemv_mma")
-    ap.add_argument("--mode", default="streaming", choices=["streaming", "dependent", "serial"])
+    ap.add_argument("--mode", default="independent",
+                    choices=["independent", "inputs-ready", "chained", "serial"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--context-reps", type=int, default=200,
@@ -241,8 +244,10 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     ext = build("int4gemv")
-    mode_flags = {"streaming": nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY,
-                  "dependent": nat.CL_LAUNCH_PDL, "serial": 0}
+    mode_flags = {"independent": nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY
+                  | nat.CL_LAUNCH_OUTPUTS_FREE,
+                  "inputs-ready": nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY,
+                  "chained": nat.CL_LAUNCH_PDL, "serial": 0}
     flags = mode_flags[args.mode]
     pool = op.make_bench_pool(N_ROWS, K_COLS, mode="l2cold", pool_size=POOL, weight_dist=0.02)
 

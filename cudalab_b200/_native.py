@@ -20,6 +20,7 @@ CL_ERR_DEVICE_TIMEOUT = 5
 
 CL_LAUNCH_PDL = 1
 CL_LAUNCH_INPUTS_READY = 2
+CL_LAUNCH_OUTPUTS_FREE = 4
 
 CL_VARIANTS_NORMAL = 0
 CL_VARIANTS_ALL = 1

@@ -344,6 +344,7 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
     g.x_stride = a.x_stride;
     g.y_stride = a.y_stride;
     g.early_x = (flags & 3u) == 3u ? 1 : 0;
+    g.free_y = (!kPeer && (flags & 7u) == 7u) ? 1 : 0;
     const bool all_full = (g.blocks % kMmaChunkBlocks) == 0;
     using S = typename Fmt::Scale;
     auto go = [&](auto kernel) -> cudaError_t {
@@ -369,12 +370,13 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
             if (clusters <= 0) return cudaErrorInvalidConfiguration;
             if (clusters < g.groups) {
                 const int64_t x_stride = g.x_stride, y_stride = g.y_stride;
-                const int early = g.early_x;
+                const int early = g.early_x, free_y = g.free_y;
                 if (!make_mma_geom(a.N, a.K, a.M, kInt4, sm_count(dev), kCtasPerSm, clusters, g))
                     return cudaErrorInvalidConfiguration;
                 g.x_stride = x_stride;
                 g.y_stride = y_stride;
                 g.early_x = early;
+                g.free_y = free_y;
                 smem = mma_smem_total(g);
                 if ((err = ensure_smem_attr(kernel, dev, smem)) != cudaSuccess) return err;
             }
@@ -434,7 +436,8 @@ cudaError_t launch_mma_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
         return (flags & 3u) == 3u ? launch_mma<Fmt, 8, 1>(a, s, flags)
                                   : launch_mma<Fmt, 8, 2>(a, s, flags);
     if ((flags & 3u) == 3u)
-        return a.K <= 16384 ? launch_mma<Fmt, 4, 1>(a, s, flags) : launch_mma<Fmt, 8, 1>(a, s, flags);
+        return a.K <= 16384 ? launch_mma<Fmt, 4, 1>(a, s, flags)
+                            : launch_mma<Fmt, 8, 1>(a, s, flags);
     return a.K <= 2048 ? launch_mma<Fmt, 8, 1>(a, s, flags) : launch_mma<Fmt, 8, 2>(a, s, flags);
 }
 
@@ -459,6 +462,7 @@ const VariantDesc kInt4Variants[] = {
     {"int4gemv_ldg", per_row<launch_vec1<Int4Fmt, MathF16, false>>, false},
     {"int4gemv_ldg_f32x2", per_row<launch_vec1<Int4Fmt, MathF32x2, false>>, false},
     {"int4gemv_mma", launch_mma_auto<MmaInt4>, false},
+    {"int4gemv_mma_w2", launch_mma<MmaInt4, 2, 1>, false},
     {"int4gemv_mma_w4", launch_mma<MmaInt4, 4, 1>, false},
     {"int4gemv_mma_w8", launch_mma<MmaInt4, 8, 1>, false},
     {"int4gemv_mma_w8c2", launch_mma<MmaInt4, 8, 2>, false},
@@ -472,6 +476,7 @@ const VariantDesc kInt8Variants[] = {
     {"qgemv_ldg", per_row<launch_vec1<Int8Fmt, MathF16, false>>, false},
     {"qgemv_ldg_f32x2", per_row<launch_vec1<Int8Fmt, MathF32x2, false>>, false},
     {"qgemv_mma", launch_mma_auto<MmaInt8>, false},
+    {"qgemv_mma_w2", launch_mma<MmaInt8, 2, 1>, false},
     {"qgemv_mma_w4", launch_mma<MmaInt8, 4, 1>, false},
     {"qgemv_mma_w8", launch_mma<MmaInt8, 8, 1>, false},
     {"qgemv_mma_w8c2", launch_mma<MmaInt8, 8, 2>, false},

@@ -76,6 +76,7 @@ struct MmaGeom {
     int32_t part_floats;          // partial buffer size
     int32_t max_rows;             // rows of the largest row group
     int32_t early_x;              // x is not written by the preceding kernel
+    int32_t free_y;               // y is not accessed by any kernel still in flight
 };
 
 constexpr int kZeroRegion = 256;  // bytes of zeros ahead of the staged activations
@@ -578,8 +579,12 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
         }
     };
     // y may be read or written by the preceding kernel: store only after it.
+    // With free_y (y untouched by every kernel still in flight) the stores do
+    // not wait; CTA 0 alone waits for the preceding kernel, at its very end,
+    // so that this grid still completes after it (completion order, and with
+    // it the visibility guarantees of the stream, stay transitive).
     auto make_ready = [&]() {
-        if (g.early_x) pdl_wait_prior_grids();
+        if (g.early_x && !(kPeer == false && g.free_y)) pdl_wait_prior_grids();
         if constexpr (kPeer) {
             // the step number, written by the preceding step's last CTA (complete now)
             if (tid == 0)
@@ -664,6 +669,8 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     if constexpr (kPeer) {
         __syncthreads();
         if (tid == 0) peer_arrive_and_wait(po, epoch);
+    } else {
+        if (g.free_y && blockIdx.x == 0) pdl_wait_prior_grids();
     }
 }
 

@@ -53,6 +53,15 @@ extern "C" {
  * x and compute before waiting on the preceding kernel and wait only before
  * storing y.  Ignored by variants that do not use it. */
 #define CL_LAUNCH_INPUTS_READY 2u
+/* Together with CL_LAUNCH_PDL | CL_LAUNCH_INPUTS_READY: y is not read or
+ * written by any kernel that may still be running when this GEMV starts
+ * (independent output buffers, e.g. the q / k / v projections of one
+ * activation, or a stream of independent GEMVs).  The tensor-core variants
+ * then store y without waiting; one CTA still waits for the preceding kernel,
+ * so the GEMV completes after it and the stream's completion order (and what
+ * later kernels may rely on) is unchanged.  Ignored by the sharded entry
+ * points and by variants that do not use it. */
+#define CL_LAUNCH_OUTPUTS_FREE 4u
 
 /* ---- variant list selectors ---- */
 #define CL_VARIANTS_NORMAL 0 /* dispatchable variants */

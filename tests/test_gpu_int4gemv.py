@@ -97,7 +97,10 @@ def test_deterministic_and_pdl_identical(ext, variant):
     y1 = ext.forward(variant, Wp, s, x)
     y2 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL)
     y3 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY)
+    y4 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY
+                     | nat.CL_LAUNCH_OUTPUTS_FREE)
     assert torch.equal(y0, y1) and torch.equal(y0, y2) and torch.equal(y0, y3)
+    assert torch.equal(y0, y4)
 
 
 def test_graph_capture_matches_eager(ext):
@@ -192,3 +195,47 @@ def test_sharded_fused_single_rank(ext, one_rank_group, variant, flags):
         assert nat.device_status(clear=True) == 0
     finally:
         sg.close()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_outputs_free_chain_completes_in_order(ext, graph):
+    """A chain of independent GEMVs launched with PDL | INPUTS_READY |
+    OUTPUTS_FREE (only one CTA of each waits for its predecessor), a slow one
+    first, then a plain consumer kernel: the consumer must see every output
+    (buffers start as NaN, so a stale read is detected)."""
+    flags = nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY | nat.CL_LAUNCH_OUTPUTS_FREE
+    shapes = [(28672, 8192)] + [(1024, 4096)] * 7
+    ws = [make_w4(N, K, seed=200 + i)[:2] for i, (N, K) in enumerate(shapes)]
+    xs = [make_x4(K, seed=300 + i) for i, (N, K) in enumerate(shapes)]
+    ref = [ext.forward("int4gemv_mma", w, sc, x) for (w, sc), x in zip(ws, xs)]
+    outs = [torch.empty(N, dtype=torch.float16, device="cuda") for N, _ in shapes]
+    st = torch.cuda.Stream()
+
+    def chain():
+        for (w, sc), x, o in zip(ws, xs, outs):
+            ext.forward_into("int4gemv_mma", w, sc, x, o, flags=flags)
+        return torch.cat(outs)  # plain kernels reading every output
+
+    for _ in range(3 if graph else 20):
+        for o in outs:
+            o.fill_(float("nan"))
+        torch.cuda.synchronize()
+        if graph:
+            with torch.cuda.stream(st):
+                chain()
+            st.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                got = chain()
+            for o in outs:
+                o.fill_(float("nan"))
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            del g
+        else:
+            with torch.cuda.stream(st):
+                got = chain()
+            st.synchronize()
+        assert torch.equal(got, torch.cat(ref))
+    assert nat.device_status(clear=True) == 0
