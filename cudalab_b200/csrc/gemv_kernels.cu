@@ -296,11 +296,22 @@ bool make_mma_geom(int64_t N, int64_t K, int64_t M, bool int4, int num_sms, int 
     g.tiles_rem = (int32_t)(tiles % groups);
     const int64_t max_tiles = g.tiles_base + (g.tiles_rem > 0 ? 1 : 0);
     g.max_rows = (int32_t)std::min<int64_t>(16 * max_tiles, N);
+    // Segments (M > 1): runs of seg_chunks consecutive chunks of one tile
+    // summed by one warp into one partial slot, long only when the grid has
+    // many more items than warps (16 x SMs); M = 1 keeps one chunk per slot.
+    // The length, like the split, depends on the shape only, so the summation
+    // order does too.
+    const int64_t seg_max = M == 1 ? 1
+                                   : std::max<int64_t>(1, std::min<int64_t>(
+                                         kc_split, tiles * g.n_kc / (16 * (int64_t)num_sms)));
+    const int64_t n_seg = (kc_split + seg_max - 1) / seg_max;
+    const int64_t seg = (kc_split + n_seg - 1) / n_seg;  // balanced lengths
+    g.seg_chunks = (int32_t)seg;
     const int64_t part_budget = (M == 1 ? 32 : M <= 8 ? 24 : 48) * 1024;
-    const int64_t per_tile = kc_split * 16 * M * 4;
+    const int64_t per_tile = n_seg * 16 * M * 4;
     const int64_t rt = std::max<int64_t>(1, std::min<int64_t>(max_tiles, part_budget / per_tile));
     g.round_tiles = (int32_t)rt;
-    g.part_floats = (int32_t)(rt * kc_split * 16 * M);
+    g.part_floats = (int32_t)(rt * n_seg * 16 * M);
     return mma_smem_total(g) <= 226 * 1024;  // 1 KiB left for static shared memory
 }
 

@@ -71,6 +71,7 @@ struct MmaGeom {
     int32_t tiles_base, tiles_rem;  // tiles per row group (balanced)
     int32_t splits;               // K splits (cluster size when > 1)
     int32_t kc_split;             // chunks per split (the last split may have fewer)
+    int32_t seg_chunks;           // chunks per segment (one warp, one partial slot)
     int32_t round_tiles;          // tiles per round of the partial buffer
     int32_t xs_words;             // staged 16-byte words per activation row
     int32_t part_floats;          // partial buffer size
@@ -230,7 +231,7 @@ struct MmaItemRegs {
     __half sa[kMmaChunkBlocks], sb[kMmaChunkBlocks];
 };
 
-// Position of a warp's current item: tile and local chunk.
+// An item: tile and chunk (relative to the split).
 struct MmaCursor {
     int tile, kc;
 };
@@ -288,14 +289,64 @@ __device__ __forceinline__ void mma_fetch(MmaItemRegs& r, const uint8_t* W,
     }
 }
 
-// Compute one item and store its partials: slot `slot` of the partial buffer
-// holds 16 rows x M floats (row-major; M = 1 for kNB = 0).
+// Running sums of one segment (consecutive chunks of one tile, computed by one
+// warp).  M = 1: v[0][0] / v[0][1] = rows g / g + 8 of this lane's columns;
+// M > 1: rows g, g+8 x columns 8j + 2t, 8j + 2t + 1 (mma accumulator layout).
+template <int kNB>
+struct MmaAcc {
+    float v[kNB == 0 ? 1 : kNB][4];
+};
+
+template <int kNB>
+__device__ __forceinline__ void mma_acc_zero(MmaAcc<kNB>& a) {
+#pragma unroll
+    for (int j = 0; j < (kNB == 0 ? 1 : kNB); ++j) a.v[j][0] = a.v[j][1] = a.v[j][2] = a.v[j][3] = 0.f;
+}
+
+// Store a finished segment's sums into slot `slot` of the partial buffer
+// (16 rows x max(M, 1) floats, row-major) and reset them.
+template <class Fmt, int kNB>
+__device__ __forceinline__ void mma_flush(MmaAcc<kNB>& acc, const MmaGeom& g, int gq, int t,
+                                          float* part, int slot) {
+    if constexpr (kNB == 0) {
+        float a = acc.v[0][0], b = acc.v[0][1];
+        if constexpr (Fmt::kGroupScale) {
+            // lane t < 2 holds the scaled sums of columns (blocks) 2t, 2t + 1;
+            // lanes t >= 2 hold the zero columns
+            if (t >= 2) a = b = 0.f;
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            b += __shfl_xor_sync(0xffffffffu, b, 1);
+        }
+        if (t == 0) {
+            float* pp = part + slot * 16;
+            pp[gq] = a;
+            pp[gq + 8] = b;
+        }
+    } else {
+        float* pp = part + slot * 16 * g.M;
+#pragma unroll
+        for (int j = 0; j < kNB; ++j) {
+            const int c = 8 * j + 2 * t;
+            if (c < g.M) {
+                pp[gq * g.M + c] = acc.v[j][0];
+                pp[(gq + 8) * g.M + c] = acc.v[j][2];
+            }
+            if (c + 1 < g.M) {
+                pp[gq * g.M + c + 1] = acc.v[j][1];
+                pp[(gq + 8) * g.M + c + 1] = acc.v[j][3];
+            }
+        }
+    }
+    mma_acc_zero<kNB>(acc);
+}
+
+// Compute one item and add it to the segment's sums.
 //   xs: staged activations of this split (row m at xs + m * xs_words);
 //   lb0: the item's first block relative to the split.
 template <class Fmt, int kNB, bool kFull>
 __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs,
                                            const uint4* zero, int lb0, int nb, const MmaGeom& g,
-                                           int gq, int t, float* part, int slot) {
+                                           int gq, int t, MmaAcc<kNB>& sacc) {
     constexpr int kBlk = Fmt::kBlockWords;
     if constexpr (kNB == 0) {
         float acc[Fmt::kAcc][4];
@@ -335,25 +386,16 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
                 }
             }
         }
-        float acc_a, acc_b;
         if constexpr (Fmt::kGroupScale) {
             // lane t < 2 holds columns (blocks) 2t (even accumulator, entries 0 / 2)
-            // and 2t + 1 (odd accumulator, entries 1 / 3); lanes t >= 2 hold zeros
+            // and 2t + 1 (odd accumulator, entries 1 / 3)
             const float sa0 = __half2float(r.sa[0]), sa1 = __half2float(r.sa[1]);
             const float sb0 = __half2float(r.sb[0]), sb1 = __half2float(r.sb[1]);
-            acc_a = fmaf(sa1, acc[1][1], sa0 * acc[0][0]);
-            acc_b = fmaf(sb1, acc[1][3], sb0 * acc[0][2]);
-            if (t >= 2) acc_a = acc_b = 0.f;
-            acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
-            acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+            sacc.v[0][0] += fmaf(sa1, acc[1][1], sa0 * acc[0][0]);
+            sacc.v[0][1] += fmaf(sb1, acc[1][3], sb0 * acc[0][2]);
         } else {
-            acc_a = acc[0][0] + acc[1][0];
-            acc_b = acc[0][2] + acc[1][2];
-        }
-        if (t == 0) {
-            float* pp = part + slot * 16;
-            pp[gq] = acc_a;
-            pp[gq + 8] = acc_b;
+            sacc.v[0][0] += acc[0][0] + acc[1][0];
+            sacc.v[0][1] += acc[0][2] + acc[1][2];
         }
     } else {
         // column c of column block j is activation row 8j + c
@@ -361,9 +403,7 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
 #pragma unroll
         for (int j = 0; j < kNB; ++j)
             bp[j] = 8 * j + gq < g.M ? xs + (8 * j + gq) * g.xs_words : nullptr;
-        float out[kNB][4];
-#pragma unroll
-        for (int j = 0; j < kNB; ++j) out[j][0] = out[j][1] = out[j][2] = out[j][3] = 0.f;
+        float (&out)[kNB][4] = sacc.v;
 #pragma unroll
         for (int q = 0; q < kMmaChunkBlocks; ++q) {
             if (kFull || q < nb) {
@@ -423,31 +463,41 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
                 }
             }
         }
-        // lane (g, t): rows g, g+8 x columns 8j + 2t, 8j + 2t + 1
-        float* pp = part + slot * 16 * g.M;
-#pragma unroll
-        for (int j = 0; j < kNB; ++j) {
-            const int c = 8 * j + 2 * t;
-            if (c < g.M) {
-                pp[gq * g.M + c] = out[j][0];
-                pp[(gq + 8) * g.M + c] = out[j][2];
-            }
-            if (c + 1 < g.M) {
-                pp[gq * g.M + c + 1] = out[j][1];
-                pp[(gq + 8) * g.M + c + 1] = out[j][3];
-            }
-        }
     }
 }
 
 template <class Fmt, int kNB, bool kAllFull>
 __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, const uint4* zero,
                                          int lb0, int blocks_left, const MmaGeom& g, int gq,
-                                         int t, float* part, int slot) {
+                                         int t, MmaAcc<kNB>& sacc) {
     if (kAllFull || blocks_left >= kMmaChunkBlocks)
-        mma_item_t<Fmt, kNB, true>(r, xs, zero, lb0, kMmaChunkBlocks, g, gq, t, part, slot);
+        mma_item_t<Fmt, kNB, true>(r, xs, zero, lb0, kMmaChunkBlocks, g, gq, t, sacc);
     else
-        mma_item_t<Fmt, kNB, false>(r, xs, zero, lb0, blocks_left, g, gq, t, part, slot);
+        mma_item_t<Fmt, kNB, false>(r, xs, zero, lb0, blocks_left, g, gq, t, sacc);
+}
+
+// A warp's position: segment (tile, seg) and chunk j inside it.  Segments of
+// a CTA are dealt to its warps round-robin in (tile, seg) order; a segment is
+// G consecutive chunks of one tile (fewer for the last one).
+struct MmaSegCursor {
+    int tile, seg, j;
+};
+
+__device__ __forceinline__ int seg_len(int seg, int G, int n_kc) { return min(G, n_kc - seg * G); }
+
+__device__ __forceinline__ void seg_normalize(MmaSegCursor& c, int n_seg) {
+    while (c.seg >= n_seg) {
+        c.seg -= n_seg;
+        ++c.tile;
+    }
+}
+
+__device__ __forceinline__ void seg_advance(MmaSegCursor& c, int G, int n_kc, int n_seg,
+                                            int step) {
+    if (++c.j < seg_len(c.seg, G, n_kc)) return;
+    c.j = 0;
+    c.seg += step;
+    seg_normalize(c, n_seg);
 }
 
 // ---------------------------------------------------------------------------
@@ -489,18 +539,22 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     const uint64_t pol = policy_evict_first();
 
     pdl_allow_dependents();
-    // Items of this warp: w, w + kWarps, ... in (tile, chunk) order.  Weights
-    // and scales never depend on the preceding kernel: the first two items
-    // are requested before waiting on it.
-    MmaCursor ca{0, warp};
-    cursor_advance(ca, 0, n_kc);
-    MmaCursor cb = ca;
-    cursor_advance(cb, kWarps, n_kc);
+    // Segments of this warp: w, w + kWarps, ... in (tile, seg) order, each
+    // walked chunk by chunk.  Weights and scales never depend on the preceding
+    // kernel: the first two items are requested before waiting on it.
+    const int G = g.seg_chunks;
+    const int n_seg = (n_kc + G - 1) / G;
+    MmaSegCursor ca{0, warp, 0};
+    seg_normalize(ca, n_seg);
+    MmaSegCursor cb = ca;
+    seg_advance(cb, G, n_kc, n_seg, kWarps);
     MmaItemRegs ra, rb;
     if (ca.tile < n_tiles)
-        mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0, ca, gq, t, pol);
+        mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0,
+                                      MmaCursor{ca.tile, ca.seg * G + ca.j}, gq, t, pol);
     if (cb.tile < n_tiles)
-        mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0, cb, gq, t, pol);
+        mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0,
+                                      MmaCursor{cb.tile, cb.seg * G + cb.j}, gq, t, pol);
     if constexpr (!Fmt::kGroupScale) {
         for (int r = tid; r < nrows; r += kThreads)
             sc8[r] = reinterpret_cast<const float*>(scale)[r0 + r];
@@ -603,9 +657,9 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
         if (g.splits == 1 && !ready) make_ready();
         for (int m = 0; m < M; ++m) {
             for (int r = row_lo + tid; r < row_hi; r += kThreads) {
-                const float* pp = part + ((r >> 4) - tile0) * n_kc * 16 * M + (r & 15) * M + m;
+                const float* pp = part + ((r >> 4) - tile0) * n_seg * 16 * M + (r & 15) * M + m;
                 float s = 0.f;
-                for (int kc = 0; kc < n_kc; ++kc) s += pp[kc * 16 * M];
+                for (int sg = 0; sg < n_seg; ++sg) s += pp[sg * 16 * M];
                 if (g.splits == 1) {
                     if constexpr (!Fmt::kGroupScale) s *= sc8[r];
                     store(r, m, s);
@@ -620,32 +674,69 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     };
 
     // Ping-pong over two register buffers: compute one item while the other
-    // loads.  Every warp passes exactly n_rounds round ends.
-    for (;;) {
-        while (rnd < n_rounds && !(ca.tile < tile_end)) end_round();
-        if (rnd >= n_rounds) break;
-        {
-            const int lb0 = kMmaChunkBlocks * ca.kc;
-            mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, part,
-                                         (ca.tile - rnd * RT) * n_kc + ca.kc);
+    // loads.  A segment's last item stores the segment's sums (M = 1: every
+    // item is its own segment).  Every warp passes exactly n_rounds round ends.
+    MmaAcc<kNB> sacc;
+    mma_acc_zero<kNB>(sacc);
+    if constexpr (kNB == 0) {
+        MmaCursor ia{ca.tile, ca.seg}, ib{cb.tile, cb.seg};  // G = 1: seg == chunk
+        for (;;) {
+            while (rnd < n_rounds && !(ia.tile < tile_end)) end_round();
+            if (rnd >= n_rounds) break;
+            {
+                const int lb0 = kMmaChunkBlocks * ia.kc;
+                mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+                mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ia.tile - rnd * RT) * n_seg + ia.kc);
+            }
+            MmaCursor ic = ib;
+            cursor_advance(ic, kWarps, n_kc);
+            if (ic.tile < n_tiles)
+                mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0, ic, gq, t, pol);
+            while (rnd < n_rounds && !(ib.tile < tile_end)) end_round();
+            if (rnd >= n_rounds) break;
+            {
+                const int lb0 = kMmaChunkBlocks * ib.kc;
+                mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+                mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ib.tile - rnd * RT) * n_seg + ib.kc);
+            }
+            MmaCursor id = ic;
+            cursor_advance(id, kWarps, n_kc);
+            if (id.tile < n_tiles)
+                mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0, id, gq, t, pol);
+            ia = ic;
+            ib = id;
         }
-        MmaCursor cc = cb;
-        cursor_advance(cc, kWarps, n_kc);
-        if (cc.tile < n_tiles)
-            mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0, cc, gq, t, pol);
-        while (rnd < n_rounds && !(cb.tile < tile_end)) end_round();
-        if (rnd >= n_rounds) break;
-        {
-            const int lb0 = kMmaChunkBlocks * cb.kc;
-            mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, part,
-                                         (cb.tile - rnd * RT) * n_kc + cb.kc);
+    } else {
+        for (;;) {
+            while (rnd < n_rounds && !(ca.tile < tile_end)) end_round();
+            if (rnd >= n_rounds) break;
+            {
+                const int lb0 = kMmaChunkBlocks * (ca.seg * G + ca.j);
+                mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+                if (ca.j + 1 == seg_len(ca.seg, G, n_kc))
+                    mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ca.tile - rnd * RT) * n_seg + ca.seg);
+            }
+            MmaSegCursor cc = cb;
+            seg_advance(cc, G, n_kc, n_seg, kWarps);
+            if (cc.tile < n_tiles)
+                mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0,
+                                              MmaCursor{cc.tile, cc.seg * G + cc.j}, gq, t, pol);
+            while (rnd < n_rounds && !(cb.tile < tile_end)) end_round();
+            if (rnd >= n_rounds) break;
+            {
+                const int lb0 = kMmaChunkBlocks * (cb.seg * G + cb.j);
+                mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+                if (cb.j + 1 == seg_len(cb.seg, G, n_kc))
+                    mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (cb.tile - rnd * RT) * n_seg + cb.seg);
+            }
+            MmaSegCursor cd = cc;
+            seg_advance(cd, G, n_kc, n_seg, kWarps);
+            if (cd.tile < n_tiles)
+                mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0,
+                                              MmaCursor{cd.tile, cd.seg * G + cd.j}, gq, t, pol);
+            ca = cc;
+            cb = cd;
         }
-        MmaCursor cd = cc;
-        cursor_advance(cd, kWarps, n_kc);
-        if (cd.tile < n_tiles)
-            mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0, cd, gq, t, pol);
-        ca = cc;
-        cb = cd;
     }
 
     if (g.splits > 1) {

@@ -244,6 +244,9 @@ class ShardedGemv:
         x = x.contiguous()
         self.epoch += 1
         if self.mode == "nccl":
+            # the local shard buffer is read by the previous step's all-gather,
+            # so its GEMV must wait before storing
+            flags &= ~nat.CL_LAUNCH_OUTPUTS_FREE
             if x.dim() == 1:
                 self.ext.forward_into(self.variant, self.W, self.scale, x,
                                       self.y_shard[0, : self.n], flags=flags)
