@@ -61,6 +61,8 @@ PROTOTYPES = {
     "cl_qgemv_sharded": (_int, [_cs, _vp, _vp, _vp, _i64, _vp, _vp, _int, _int, _i64, _i64,
                                 _i64, _i64, _vp, _u32]),
     "cl_int4gemv_batched": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u32]),
+    "cl_int4gemv_quantize": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "cl_qgemv_quantize": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "cl_qgemv_batched": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u32]),
 }
 

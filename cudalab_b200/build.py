@@ -33,7 +33,7 @@ HEADER = ROOT / "include" / "cudalab_gemv.h"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared"]
-SOURCES = ["gemv_kernels.cu", "capi.cu"]
+SOURCES = ["gemv_kernels.cu", "quantize.cu", "capi.cu"]
 
 
 def _nvcc() -> str:

@@ -15,6 +15,7 @@
 
 #include "../../include/cudalab_gemv.h"
 #include "gemv_launch.h"
+#include "gemv_quantize.h"
 
 namespace {
 
@@ -311,6 +312,36 @@ int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed)
     int n = 0;
     const clb::VariantDesc* t = clb::int8_variants(&n);
     return list_variants(t, n, which, buf, buf_len, needed);
+}
+
+// ---- quantisation ----
+int cl_int4gemv_quantize(const void* W, int64_t N, int64_t K, uint8_t* W_packed, void* scale,
+                         void* stream) {
+    if (N <= 0 || K <= 0) return fail(CL_ERR_INVALID_ARGUMENT, "int4gemv_quantize: N, K must be > 0");
+    if (K % 128 != 0)
+        return fail(CL_ERR_INVALID_ARGUMENT,
+                    "int4gemv_quantize: K must be divisible by 128 (group_size=128)");
+    if (!W || !W_packed || !scale)
+        return fail(CL_ERR_INVALID_ARGUMENT, "int4gemv_quantize: null device pointer");
+    if (reinterpret_cast<uintptr_t>(W) & 7u)
+        return fail(CL_ERR_INVALID_ARGUMENT, "int4gemv_quantize: W must be 8-byte aligned");
+    cudaError_t e = clb::launch_int4_quantize(W, N, K, W_packed, scale,
+                                              static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "int4gemv_quantize launch");
+    return CL_OK;
+}
+
+int cl_qgemv_quantize(const void* W, int64_t N, int64_t K, int8_t* W_q, float* scale,
+                      void* stream) {
+    if (N <= 0 || K <= 0) return fail(CL_ERR_INVALID_ARGUMENT, "qgemv_quantize: N, K must be > 0");
+    if (N > ((int64_t)1 << 31) - 1)
+        return fail(CL_ERR_INVALID_ARGUMENT, "qgemv_quantize: N exceeds 2^31 - 1 rows");
+    if (!W || !W_q || !scale)
+        return fail(CL_ERR_INVALID_ARGUMENT, "qgemv_quantize: null device pointer");
+    cudaError_t e = clb::launch_int8_quantize(W, N, K, W_q, scale,
+                                              static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "qgemv_quantize launch");
+    return CL_OK;
 }
 
 // ---- peer buffers and the row-sharded GEMV ----

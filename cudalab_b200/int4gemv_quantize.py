@@ -56,6 +56,24 @@ def quantize_w(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return W_packed, s32.to(torch.float16).contiguous()
 
 
+def quantize_w_device(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quantize_w on the GPU through the C ABI (cl_int4gemv_quantize): the same
+    checks and the same bytes, one pass over W on the current stream."""
+    _check_w(W)
+    _require(W.is_cuda, "quantize_w_device requires a CUDA tensor")
+    from . import _native as nat
+    lib = nat.load()
+    N, K = W.shape
+    Wp = torch.empty(N, K // 2, dtype=torch.uint8, device=W.device)
+    s = torch.empty(N, K // GROUP_SIZE, dtype=torch.float16, device=W.device)
+    with torch.cuda.device(W.device):
+        rc = lib.cl_int4gemv_quantize(W.data_ptr(), N, K, Wp.data_ptr(), s.data_ptr(),
+                                      torch.cuda.current_stream(W.device).cuda_stream)
+    if rc != nat.CL_OK:
+        raise RuntimeError(f"cl_int4gemv_quantize failed ({rc}): {nat.last_error(lib)}")
+    return Wp, s
+
+
 def pack_q(q: torch.Tensor) -> torch.Tensor:
     """int [N, K] with values in [-8, 7] -> uint8 [N, K/2] (low nibble = even k).
     Follows cudalab/int4gemv_quantize.py:92-114."""

@@ -34,6 +34,27 @@ def quantize_w(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q.to(torch.int8), scale
 
 
+def quantize_w_device(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quantize_w on the GPU through the C ABI (cl_qgemv_quantize): the same
+    checks and the same bytes."""
+    _require(W.dim() == 2, f"expected a 2-D W (N, K), got {W.dim()}-D")
+    _require(W.dtype == torch.float16, f"quantize_w accepts fp16 weights only, got {W.dtype}")
+    _require(W.is_contiguous(), "quantize_w requires a contiguous W")
+    _require(bool(torch.isfinite(W).all()), "quantize_w requires finite W (no NaN/Inf)")
+    _require(W.is_cuda, "quantize_w_device requires a CUDA tensor")
+    from . import _native as nat
+    lib = nat.load()
+    N, K = W.shape
+    Wq = torch.empty(N, K, dtype=torch.int8, device=W.device)
+    s = torch.empty(N, dtype=torch.float32, device=W.device)
+    with torch.cuda.device(W.device):
+        rc = lib.cl_qgemv_quantize(W.data_ptr(), N, K, Wq.data_ptr(), s.data_ptr(),
+                                   torch.cuda.current_stream(W.device).cuda_stream)
+    if rc != nat.CL_OK:
+        raise RuntimeError(f"cl_qgemv_quantize failed ({rc}): {nat.last_error(lib)}")
+    return Wq, s
+
+
 def dequantize_w(W_q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     """fp32 [N, K] = W_q * scale[:, None] (cudalab/qgemv_quantize.py:67-70)."""
     return W_q.float() * scale.unsqueeze(1)

@@ -142,6 +142,19 @@ int cl_qgemv_native_timing(const char* variant, const int8_t* W_q, const float* 
  * kernels/qgemv/bindings.cpp:281-306. */
 int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
 
+/* ---- quantisation on the device ----
+ * Replace the offline torch quantisers quantize_w of
+ * cudalab/int4gemv_quantize.py:61-114 (INT4: group 128, scale fp16 =
+ * fp32 amax / 7, q = clamp(round_half_even(W / scale), -7, 7), packed two per
+ * byte, low nibble = even k) and cudalab/qgemv_quantize.py:33-64 (INT8: scale
+ * fp32 = row amax / 127, q = clamp(round_half_even(W / scale), -127, 127)),
+ * byte for byte.  W is fp16 [N, K], row-major, finite; W is 8-byte aligned
+ * for INT4. */
+int cl_int4gemv_quantize(const void* W, int64_t N, int64_t K, uint8_t* W_packed, void* scale,
+                         void* stream);
+int cl_qgemv_quantize(const void* W, int64_t N, int64_t K, int8_t* W_q, float* scale,
+                      void* stream);
+
 /* ---- row-sharded GEMV over the GPUs of one node (one process per GPU) ----
  *
  * Rows of W are split into contiguous shards, one per rank; x is replicated;
