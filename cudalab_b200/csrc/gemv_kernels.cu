@@ -432,33 +432,44 @@ cudaError_t launch_mma_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream
 }
 
 // Geometry chosen per call (measured on B200 with L2-cold pools):
-//  * independent GEMVs (CL_LAUNCH_PDL | CL_LAUNCH_INPUTS_READY): 4-warp CTAs,
-//    one per SM per GEMV, so up to four GEMVs overlap on an SM; 8-warp CTAs
-//    once K > 16384 (the staged activations then limit co-residency);
+//  * independent GEMVs (CL_LAUNCH_PDL | CL_LAUNCH_INPUTS_READY): one CTA per
+//    SM per GEMV with 2 warps (K <= 4096: up to eight GEMVs overlap on an
+//    SM), 4 warps (K <= 16384) or 8 warps (the staged activations then limit
+//    co-residency);
 //  * chained or plain launches: 8-warp CTAs, two per SM per GEMV (shorter
 //    per-GEMV latency), one per SM for K <= 2048;
-//  * 2..8 activation rows: 8-warp CTAs (two fit on an SM), one per SM per
-//    launch for independent launches, two for chained ones;
-//  * 9..16 rows: one 16-warp CTA per SM (two column blocks need the registers).
+//  * several activation rows: one CTA per SM per launch; 4 warps (2..8 rows)
+//    or 16 warps (9..16 rows) for matrices up to 2^25 weights, 8 warps above;
+//    chained or plain launches of 2..8 rows take two 8-warp CTAs per SM.
 template <class Fmt>
 cudaError_t launch_mma_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
-    if (a.M > 8) return launch_mma<Fmt, 16, 1>(a, s, flags);
-    if (a.M > 1)
-        return (flags & 3u) == 3u ? launch_mma<Fmt, 8, 1>(a, s, flags)
-                                  : launch_mma<Fmt, 8, 2>(a, s, flags);
-    if ((flags & 3u) == 3u)
+    const bool small = a.N * a.K <= ((int64_t)1 << 25);
+    if (a.M > 8)
+        return small ? launch_mma<Fmt, 16, 1>(a, s, flags) : launch_mma<Fmt, 8, 1>(a, s, flags);
+    if (a.M > 1) {
+        if ((flags & 3u) != 3u) return launch_mma<Fmt, 8, 2>(a, s, flags);
+        return small ? launch_mma<Fmt, 4, 1>(a, s, flags) : launch_mma<Fmt, 8, 1>(a, s, flags);
+    }
+    if ((flags & 3u) == 3u) {
+        if (a.K <= 4096) return launch_mma<Fmt, 2, 1>(a, s, flags);
         return a.K <= 16384 ? launch_mma<Fmt, 4, 1>(a, s, flags)
                             : launch_mma<Fmt, 8, 1>(a, s, flags);
+    }
     return a.K <= 2048 ? launch_mma<Fmt, 8, 1>(a, s, flags) : launch_mma<Fmt, 8, 2>(a, s, flags);
 }
 
 template <class Fmt>
 cudaError_t launch_mma_sharded_auto(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
                                     unsigned flags) {
-    if (a.M > 8) return launch_mma_sharded<Fmt, 16, 1>(a, pa, s, flags);
-    if (a.M > 1)
-        return (flags & 3u) == 3u ? launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags)
-                                  : launch_mma_sharded<Fmt, 8, 2>(a, pa, s, flags);
+    const bool small = a.N * a.K <= ((int64_t)1 << 25);
+    if (a.M > 8)
+        return small ? launch_mma_sharded<Fmt, 16, 1>(a, pa, s, flags)
+                     : launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags);
+    if (a.M > 1) {
+        if ((flags & 3u) != 3u) return launch_mma_sharded<Fmt, 8, 2>(a, pa, s, flags);
+        return small ? launch_mma_sharded<Fmt, 4, 1>(a, pa, s, flags)
+                     : launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags);
+    }
     if ((flags & 3u) == 3u)
         return a.K <= 16384 ? launch_mma_sharded<Fmt, 4, 1>(a, pa, s, flags)
                             : launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags);
