@@ -356,7 +356,11 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
     g.y_stride = a.y_stride;
     g.early_x = (flags & 3u) == 3u ? 1 : 0;
     g.free_y = (!kPeer && (flags & 7u) == 7u) ? 1 : 0;
-    const bool all_full = (g.blocks % kMmaChunkBlocks) == 0;
+    // Whole-chunk rows, (INT4) scale rows 8-byte aligned for vector loads and
+    // block indices within 32 bits: fetch addresses are stepped, not recomputed.
+    const bool all_full = (g.blocks % kMmaChunkBlocks) == 0 &&
+                          (!kInt4 || (reinterpret_cast<uintptr_t>(a.scale) & 7u) == 0) &&
+                          a.N * (int64_t)g.blocks <= (int64_t)UINT32_MAX;
     using S = typename Fmt::Scale;
     auto go = [&](auto kernel) -> cudaError_t {
         int smem = mma_smem_total(g);

@@ -119,12 +119,15 @@ __device__ __forceinline__ uint32_t nib_pair_hi(uint32_t w) {
                              h2_const(kH_1_16), h2_const(kH_m72)));
 }
 
-// Formats.  kAcc: independent accumulators per item at M = 1 (blocks of even
-// / odd index), which halves the length of the dependent mma chain.
+// Formats.  kAcc: independent accumulators per item at M = 1 (block q uses
+// accumulator q % kAcc), so kAcc dependent mma chains run side by side.  INT4
+// block q only writes batch column q, so adding the accumulators of blocks
+// with the same column parity is exact (the other terms are zeros) and the
+// result does not depend on kAcc.
 struct MmaInt4 {
     static constexpr bool kGroupScale = true;
     static constexpr int kBlockWords = 16;  // 16-byte words of activations per block
-    static constexpr int kAcc = 2;
+    static constexpr int kAcc = 4;
     using Scale = __half;
 };
 struct MmaInt8 {
@@ -224,45 +227,101 @@ __device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned
 // ---------------------------------------------------------------------------
 
 // One item = 16 rows x up to 4 blocks: the fragments (rows g, g+8) and the
-// INT4 group scales of those rows.  M = 1 uses the scales of the two blocks
-// (columns) the lane holds; M > 1 all four blocks' scales.
+// INT4 group scales of those rows, two per word (block 2i in the low half of
+// word i).  M = 1 uses word 0 only: the scales of the two blocks (columns)
+// the lane holds; M > 1 all four blocks' scales.
 struct MmaItemRegs {
     uint4 wa[kMmaChunkBlocks], wb[kMmaChunkBlocks];
-    __half sa[kMmaChunkBlocks], sb[kMmaChunkBlocks];
+    uint32_t sa[2], sb[2];
 };
 
-// An item: tile and chunk (relative to the split).
-struct MmaCursor {
-    int tile, kc;
+__device__ __forceinline__ float scale_at(const uint32_t (&s)[2], int q) {
+    const uint32_t w = s[q >> 1];
+    return __half2float(__ushort_as_half((unsigned short)((q & 1) ? (w >> 16) : (w & 0xFFFFu))));
+}
+
+__device__ __forceinline__ uint32_t pack_halves(__half lo, __half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+// Where one item's loads start, as 64-byte block indices into W (and group
+// indices into the INT4 scales, the same numbers) of rows a = g and b = g + 8,
+// and the item's first block within the row.  Consecutive chunks of a row are
+// 4 blocks apart, so walking a segment only steps the indices.  Rows beyond
+// the group re-read its last row (L2 hit; their results are never stored),
+// so no load is predicated.  The launch keeps N * blocks below 2^32.
+struct MmaFetchPtr {
+    uint32_t ea, eb;
+    int blk0;
 };
 
-__device__ __forceinline__ void cursor_advance(MmaCursor& c, int step, int n_kc) {
-    c.kc += step;
-    while (c.kc >= n_kc) {
-        c.kc -= n_kc;
-        ++c.tile;
+__device__ __forceinline__ MmaFetchPtr mma_fetch_ptr(const MmaGeom& g, int64_t r0, int nrows,
+                                                     int kc0, int tile, int kc, int gq) {
+    const int last = nrows - 1;
+    const int64_t ra = r0 + min(16 * tile + gq, last);
+    const int64_t rb = r0 + min(16 * tile + gq + 8, last);
+    MmaFetchPtr p;
+    p.blk0 = kMmaChunkBlocks * (kc0 + kc);
+    p.ea = (uint32_t)(ra * g.blocks + p.blk0);
+    p.eb = (uint32_t)(rb * g.blocks + p.blk0);
+    return p;
+}
+
+__device__ __forceinline__ void mma_fetch_step(MmaFetchPtr& p) {
+    p.ea += kMmaChunkBlocks;
+    p.eb += kMmaChunkBlocks;
+    p.blk0 += kMmaChunkBlocks;
+}
+
+// Issue the loads of one item in a matrix whose rows are whole chunks (row
+// bytes a multiple of 256) with 8-byte aligned scale rows.  wl = W + 16 t (the
+// lane's 16 bytes of a block); sl = the INT4 scales, advanced by 2 (t & 1) at
+// M = 1 (the lane's first block).  The scales come as one 4-byte (M = 1) or
+// 8-byte (M > 1) load per row.
+template <class Fmt, int kNB>
+__device__ __forceinline__ void mma_fetch(MmaItemRegs& r, const MmaFetchPtr& p,
+                                          const uint8_t* wl, const __half* sl, uint64_t pol) {
+    const uint8_t* pa = wl + 64 * (size_t)p.ea;
+    const uint8_t* pb = wl + 64 * (size_t)p.eb;
+#pragma unroll
+    for (int q = 0; q < kMmaChunkBlocks; ++q) {
+        r.wa[q] = ldg_stream16(pa + 64 * q, pol);
+        r.wb[q] = ldg_stream16(pb + 64 * q, pol);
+    }
+    if constexpr (Fmt::kGroupScale) {
+        const __half* sa = sl + p.ea;
+        const __half* sb = sl + p.eb;
+        if constexpr (kNB == 0) {
+            r.sa[0] = __ldg(reinterpret_cast<const unsigned int*>(sa));
+            r.sb[0] = __ldg(reinterpret_cast<const unsigned int*>(sb));
+        } else {
+            const uint2 va = __ldg(reinterpret_cast<const uint2*>(sa));
+            const uint2 vb = __ldg(reinterpret_cast<const uint2*>(sb));
+            r.sa[0] = va.x;
+            r.sa[1] = va.y;
+            r.sb[0] = vb.x;
+            r.sb[1] = vb.y;
+        }
     }
 }
 
-// Issue the loads of one item (global chunk kc0 + c.kc).  Rows beyond the
-// group re-read its last row (L2 hit; their results are never stored), so no
-// load is predicated.  kAllFull: every chunk of a row has 4 blocks (row bytes
-// a multiple of 256); otherwise blocks past the row end re-read its last
-// block (their mma is skipped).
-template <class Fmt, int kNB, bool kAllFull>
-__device__ __forceinline__ void mma_fetch(MmaItemRegs& r, const uint8_t* W,
-                                          const typename Fmt::Scale* scale, const MmaGeom& g,
-                                          int64_t r0, int nrows, int kc0, MmaCursor c, int gq,
-                                          int t, uint64_t pol) {
+// Issue the loads of one item (tile, chunk kc of the split) in a matrix with a
+// short last chunk per row: blocks past the row end re-read the row's last
+// block (their mma is skipped).  Rows beyond the group re-read its last row.
+template <class Fmt, int kNB>
+__device__ __forceinline__ void mma_fetch_ragged(MmaItemRegs& r, const uint8_t* W,
+                                                 const typename Fmt::Scale* scale,
+                                                 const MmaGeom& g, int64_t r0, int nrows, int kc0,
+                                                 int tile, int kc, int gq, int t, uint64_t pol) {
     const int last = nrows - 1;
-    const int64_t ra = r0 + min(16 * c.tile + gq, last);
-    const int64_t rb = r0 + min(16 * c.tile + gq + 8, last);
-    const int blk0 = kMmaChunkBlocks * (kc0 + c.kc);
+    const int64_t ra = r0 + min(16 * tile + gq, last);
+    const int64_t rb = r0 + min(16 * tile + gq + 8, last);
+    const int blk0 = kMmaChunkBlocks * (kc0 + kc);
     const uint8_t* pa = W + ra * g.row_bytes + 16 * t;
     const uint8_t* pb = W + rb * g.row_bytes + 16 * t;
 #pragma unroll
     for (int q = 0; q < kMmaChunkBlocks; ++q) {
-        const int blk = kAllFull ? blk0 + q : min(blk0 + q, g.blocks - 1);
+        const int blk = min(blk0 + q, g.blocks - 1);
         r.wa[q] = ldg_stream16(pa + 64 * blk, pol);
         r.wb[q] = ldg_stream16(pb + 64 * blk, pol);
     }
@@ -271,20 +330,18 @@ __device__ __forceinline__ void mma_fetch(MmaItemRegs& r, const uint8_t* W,
         const __half* sb = reinterpret_cast<const __half*>(scale) + rb * g.blocks;
         if constexpr (kNB == 0) {
             // lane (g, t) needs the scales of blocks 2(t&1), 2(t&1)+1 of rows g, g+8
-            const int b0 = blk0 + 2 * (t & 1);
-            const int b0c = kAllFull ? b0 : min(b0, g.blocks - 1);
-            const int b1 = kAllFull ? b0 + 1 : min(b0 + 1, g.blocks - 1);
-            r.sa[0] = sa[b0c];
-            r.sa[1] = sa[b1];
-            r.sb[0] = sb[b0c];
-            r.sb[1] = sb[b1];
+            const int b0 = min(blk0 + 2 * (t & 1), g.blocks - 1);
+            const int b1 = min(blk0 + 2 * (t & 1) + 1, g.blocks - 1);
+            r.sa[0] = pack_halves(sa[b0], sa[b1]);
+            r.sb[0] = pack_halves(sb[b0], sb[b1]);
         } else {
+            int blk[kMmaChunkBlocks];
 #pragma unroll
-            for (int q = 0; q < kMmaChunkBlocks; ++q) {
-                const int blk = kAllFull ? blk0 + q : min(blk0 + q, g.blocks - 1);
-                r.sa[q] = sa[blk];
-                r.sb[q] = sb[blk];
-            }
+            for (int q = 0; q < kMmaChunkBlocks; ++q) blk[q] = min(blk0 + q, g.blocks - 1);
+            r.sa[0] = pack_halves(sa[blk[0]], sa[blk[1]]);
+            r.sa[1] = pack_halves(sa[blk[2]], sa[blk[3]]);
+            r.sb[0] = pack_halves(sb[blk[0]], sb[blk[1]]);
+            r.sb[1] = pack_halves(sb[blk[2]], sb[blk[3]]);
         }
     }
 }
@@ -364,10 +421,10 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
                     for (int w = 0; w < 4; ++w) {
                         const uint4 bb = bp[w * 4 + t];  // (x0,x4) (x1,x5) (x2,x6) (x3,x7)
                         const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
-                        mma_16816(acc[q & 1], nib_pair_lo(ua[w]), nib_pair_lo(ub[w]),
+                        mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ua[w]), nib_pair_lo(ub[w]),
                                   nib_pair_hi(ua[w]), nib_pair_hi(ub[w]), bb.x, bb.y);
-                        mma_16816(acc[q & 1], nib_pair_lo(ha), nib_pair_lo(hb), nib_pair_hi(ha),
-                                  nib_pair_hi(hb), bb.z, bb.w);
+                        mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ha), nib_pair_lo(hb),
+                                  nib_pair_hi(ha), nib_pair_hi(hb), bb.z, bb.w);
                     }
                 } else {
 #pragma unroll
@@ -378,7 +435,7 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
                             __half2 qa[2], qb[2];
                             int8x4_to_h2(ua[2 * jj + h], qa);
                             int8x4_to_h2(ub[2 * jj + h], qb);
-                            mma_16816(acc[q & 1], h2_as_u32(qa[0]), h2_as_u32(qb[0]),
+                            mma_16816(acc[q % Fmt::kAcc], h2_as_u32(qa[0]), h2_as_u32(qb[0]),
                                       h2_as_u32(qa[1]), h2_as_u32(qb[1]), h ? bb.z : bb.x,
                                       h ? bb.w : bb.y);
                         }
@@ -387,13 +444,23 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
             }
         }
         if constexpr (Fmt::kGroupScale) {
-            // lane t < 2 holds columns (blocks) 2t (even accumulator, entries 0 / 2)
-            // and 2t + 1 (odd accumulator, entries 1 / 3)
-            const float sa0 = __half2float(r.sa[0]), sa1 = __half2float(r.sa[1]);
-            const float sb0 = __half2float(r.sb[0]), sb1 = __half2float(r.sb[1]);
-            sacc.v[0][0] += fmaf(sa1, acc[1][1], sa0 * acc[0][0]);
-            sacc.v[0][1] += fmaf(sb1, acc[1][3], sb0 * acc[0][2]);
+            // lane t < 2 holds columns (blocks) 2t (even accumulators, entries
+            // 0 / 2) and 2t + 1 (odd accumulators, entries 1 / 3)
+            static_assert(Fmt::kAcc % 2 == 0, "column parity per accumulator");
+            float e0 = acc[0][0], e2 = acc[0][2], e1 = acc[1][1], e3 = acc[1][3];
+#pragma unroll
+            for (int i = 2; i < Fmt::kAcc; i += 2) {
+                e0 += acc[i][0];
+                e2 += acc[i][2];
+                e1 += acc[i + 1][1];
+                e3 += acc[i + 1][3];
+            }
+            const float sa0 = scale_at(r.sa, 0), sa1 = scale_at(r.sa, 1);
+            const float sb0 = scale_at(r.sb, 0), sb1 = scale_at(r.sb, 1);
+            sacc.v[0][0] += fmaf(sa1, e1, sa0 * e0);
+            sacc.v[0][1] += fmaf(sb1, e3, sb0 * e2);
         } else {
+            static_assert(Fmt::kAcc == 2, "INT8 sums its two accumulators");
             sacc.v[0][0] += acc[0][0] + acc[1][0];
             sacc.v[0][1] += acc[0][2] + acc[1][2];
         }
@@ -434,7 +501,7 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
                         for (int j = 0; j < kNB; ++j)
                             mma_16816(bacc[j], c0, c1, c2, c3, bb[j].z, bb[j].w);
                     }
-                    const float sa = __half2float(r.sa[q]), sb = __half2float(r.sb[q]);
+                    const float sa = scale_at(r.sa, q), sb = scale_at(r.sb, q);
 #pragma unroll
                     for (int j = 0; j < kNB; ++j) {
                         out[j][0] = fmaf(sa, bacc[j][0], out[j][0]);
@@ -492,14 +559,6 @@ __device__ __forceinline__ void seg_normalize(MmaSegCursor& c, int n_seg) {
     }
 }
 
-__device__ __forceinline__ void seg_advance(MmaSegCursor& c, int G, int n_kc, int n_seg,
-                                            int step) {
-    if (++c.j < seg_len(c.seg, G, n_kc)) return;
-    c.j = 0;
-    c.seg += step;
-    seg_normalize(c, n_seg);
-}
-
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
@@ -542,19 +601,55 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     // Segments of this warp: w, w + kWarps, ... in (tile, seg) order, each
     // walked chunk by chunk.  Weights and scales never depend on the preceding
     // kernel: the first two items are requested before waiting on it.
-    const int G = g.seg_chunks;
+    // `f` / `fp`: the next item to fetch and where its loads start; the item
+    // in a register buffer is computed two items after it was fetched.
+    // M = 1 has one chunk per segment (known at compile time).
+    const int G = kNB == 0 ? 1 : g.seg_chunks;
     const int n_seg = (n_kc + G - 1) / G;
-    MmaSegCursor ca{0, warp, 0};
-    seg_normalize(ca, n_seg);
-    MmaSegCursor cb = ca;
-    seg_advance(cb, G, n_kc, n_seg, kWarps);
+    auto seg_last = [&](const MmaSegCursor& c) {
+        return kNB == 0 || c.j + 1 == seg_len(c.seg, G, n_kc);
+    };
+    MmaSegCursor f{0, warp, 0};
+    seg_normalize(f, n_seg);
+    const uint8_t* wl = W + 16 * t;
+    const __half* sl =
+        reinterpret_cast<const __half*>(scale) + (kNB == 0 && Fmt::kGroupScale ? 2 * (t & 1) : 0);
+    MmaFetchPtr fp{};
+    if (kAllFull && f.tile < n_tiles) fp = mma_fetch_ptr(g, r0, nrows, kc0, f.tile, f.seg * G, gq);
+    // fetch item f, then step to the warp's next item (a new segment: the
+    // indices are recomputed)
+    auto fetch_next = [&](MmaItemRegs& r) {
+        if constexpr (kAllFull) {
+            mma_fetch<Fmt, kNB>(r, fp, wl, sl, pol);
+        } else {
+            mma_fetch_ragged<Fmt, kNB>(r, W, scale, g, r0, nrows, kc0, f.tile, f.seg * G + f.j, gq,
+                                       t, pol);
+        }
+        if (!seg_last(f)) {
+            ++f.j;
+            if constexpr (kAllFull) mma_fetch_step(fp);
+            return;
+        }
+        f.j = 0;
+        const int tile = f.tile;
+        f.seg += kWarps;
+        seg_normalize(f, n_seg);
+        if constexpr (kAllFull) {
+            if (f.tile == tile) {  // same rows: step the indices
+                const int d = kMmaChunkBlocks * (kc0 + f.seg * G) - fp.blk0;
+                fp.ea += d;
+                fp.eb += d;
+                fp.blk0 += d;
+            } else if (f.tile < n_tiles) {
+                fp = mma_fetch_ptr(g, r0, nrows, kc0, f.tile, f.seg * G, gq);
+            }
+        }
+    };
     MmaItemRegs ra, rb;
-    if (ca.tile < n_tiles)
-        mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0,
-                                      MmaCursor{ca.tile, ca.seg * G + ca.j}, gq, t, pol);
-    if (cb.tile < n_tiles)
-        mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0,
-                                      MmaCursor{cb.tile, cb.seg * G + cb.j}, gq, t, pol);
+    MmaSegCursor ca = f;
+    if (f.tile < n_tiles) fetch_next(ra);
+    MmaSegCursor cb = f;
+    if (f.tile < n_tiles) fetch_next(rb);
     if constexpr (!Fmt::kGroupScale) {
         for (int r = tid; r < nrows; r += kThreads)
             sc8[r] = reinterpret_cast<const float*>(scale)[r0 + r];
@@ -674,69 +769,31 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     };
 
     // Ping-pong over two register buffers: compute one item while the other
-    // loads.  A segment's last item stores the segment's sums (M = 1: every
-    // item is its own segment).  Every warp passes exactly n_rounds round ends.
+    // loads.  A segment's last item stores the segment's sums.  Every warp
+    // passes exactly n_rounds round ends.
     MmaAcc<kNB> sacc;
     mma_acc_zero<kNB>(sacc);
-    if constexpr (kNB == 0) {
-        MmaCursor ia{ca.tile, ca.seg}, ib{cb.tile, cb.seg};  // G = 1: seg == chunk
-        for (;;) {
-            while (rnd < n_rounds && !(ia.tile < tile_end)) end_round();
-            if (rnd >= n_rounds) break;
-            {
-                const int lb0 = kMmaChunkBlocks * ia.kc;
-                mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
-                mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ia.tile - rnd * RT) * n_seg + ia.kc);
-            }
-            MmaCursor ic = ib;
-            cursor_advance(ic, kWarps, n_kc);
-            if (ic.tile < n_tiles)
-                mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0, ic, gq, t, pol);
-            while (rnd < n_rounds && !(ib.tile < tile_end)) end_round();
-            if (rnd >= n_rounds) break;
-            {
-                const int lb0 = kMmaChunkBlocks * ib.kc;
-                mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
-                mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ib.tile - rnd * RT) * n_seg + ib.kc);
-            }
-            MmaCursor id = ic;
-            cursor_advance(id, kWarps, n_kc);
-            if (id.tile < n_tiles)
-                mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0, id, gq, t, pol);
-            ia = ic;
-            ib = id;
+    for (;;) {
+        while (rnd < n_rounds && !(ca.tile < tile_end)) end_round();
+        if (rnd >= n_rounds) break;
+        {
+            const int lb0 = kMmaChunkBlocks * (ca.seg * G + ca.j);
+            mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+            if (seg_last(ca))
+                mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ca.tile - rnd * RT) * n_seg + ca.seg);
         }
-    } else {
-        for (;;) {
-            while (rnd < n_rounds && !(ca.tile < tile_end)) end_round();
-            if (rnd >= n_rounds) break;
-            {
-                const int lb0 = kMmaChunkBlocks * (ca.seg * G + ca.j);
-                mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
-                if (ca.j + 1 == seg_len(ca.seg, G, n_kc))
-                    mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ca.tile - rnd * RT) * n_seg + ca.seg);
-            }
-            MmaSegCursor cc = cb;
-            seg_advance(cc, G, n_kc, n_seg, kWarps);
-            if (cc.tile < n_tiles)
-                mma_fetch<Fmt, kNB, kAllFull>(ra, W, scale, g, r0, nrows, kc0,
-                                              MmaCursor{cc.tile, cc.seg * G + cc.j}, gq, t, pol);
-            while (rnd < n_rounds && !(cb.tile < tile_end)) end_round();
-            if (rnd >= n_rounds) break;
-            {
-                const int lb0 = kMmaChunkBlocks * (cb.seg * G + cb.j);
-                mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
-                if (cb.j + 1 == seg_len(cb.seg, G, n_kc))
-                    mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (cb.tile - rnd * RT) * n_seg + cb.seg);
-            }
-            MmaSegCursor cd = cc;
-            seg_advance(cd, G, n_kc, n_seg, kWarps);
-            if (cd.tile < n_tiles)
-                mma_fetch<Fmt, kNB, kAllFull>(rb, W, scale, g, r0, nrows, kc0,
-                                              MmaCursor{cd.tile, cd.seg * G + cd.j}, gq, t, pol);
-            ca = cc;
-            cb = cd;
+        ca = f;
+        if (f.tile < n_tiles) fetch_next(ra);
+        while (rnd < n_rounds && !(cb.tile < tile_end)) end_round();
+        if (rnd >= n_rounds) break;
+        {
+            const int lb0 = kMmaChunkBlocks * (cb.seg * G + cb.j);
+            mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+            if (seg_last(cb))
+                mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (cb.tile - rnd * RT) * n_seg + cb.seg);
         }
+        cb = f;
+        if (f.tile < n_tiles) fetch_next(rb);
     }
 
     if (g.splits > 1) {

@@ -103,6 +103,33 @@ def test_deterministic_and_pdl_identical(ext, variant):
     assert torch.equal(y0, y4)
 
 
+def _misaligned_copy(s: torch.Tensor) -> torch.Tensor:
+    """The same scales in a contiguous tensor that starts 2 bytes past an
+    8-byte boundary."""
+    buf = torch.empty(s.numel() + 1, dtype=s.dtype, device=s.device)
+    out = buf[1:].view(s.shape)
+    out.copy_(s)
+    assert out.is_contiguous() and out.data_ptr() % 8 == 2
+    return out
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_misaligned_scales_same_bits(ext, M):
+    # Scale rows that are not 8-byte aligned take the kernel's per-item address
+    # path instead of the stepped vector loads; the sums are the same.
+    Wp, s, _ = make_w4(1536, 4096, seed=21)
+    s2 = _misaligned_copy(s)
+    if M == 1:
+        x = make_x4(4096, seed=22)
+        for v in ("int4gemv_mma", "int4gemv_mma_w2", "int4gemv_mma_w8c2"):
+            assert torch.equal(ext.forward(v, Wp, s, x), ext.forward(v, Wp, s2, x)), v
+    else:
+        X = torch.randn(M, 4096, generator=torch.Generator().manual_seed(23)).half().cuda()
+        for v in ("int4gemv_mma", "int4gemv_mma_w8"):
+            assert torch.equal(ext.forward_batched(v, Wp, s, X),
+                               ext.forward_batched(v, Wp, s2, X)), v
+
+
 def test_graph_capture_matches_eager(ext):
     Wps = [make_w4(1024, 2048, seed=20 + i)[:2] for i in range(4)]
     xs = [make_x4(2048, seed=40 + i) for i in range(4)]
