@@ -398,12 +398,14 @@ __device__ __forceinline__ void mma_flush(MmaAcc<kNB>& acc, const MmaGeom& g, in
 }
 
 // Compute one item and add it to the segment's sums.
-//   xs: staged activations of this split (row m at xs + m * xs_words);
+//   xs: staged activations of this split (row m at xs + m * xs_words), zero
+//       past the row end, so the blocks a short last chunk re-reads add
+//       exact zeros;
 //   lb0: the item's first block relative to the split.
-template <class Fmt, int kNB, bool kFull>
-__device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs,
-                                           const uint4* zero, int lb0, int nb, const MmaGeom& g,
-                                           int gq, int t, MmaAcc<kNB>& sacc) {
+template <class Fmt, int kNB>
+__device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, const uint4* zero,
+                                         int lb0, const MmaGeom& g, int gq, int t,
+                                         MmaAcc<kNB>& sacc) {
     constexpr int kBlk = Fmt::kBlockWords;
     if constexpr (kNB == 0) {
         float acc[Fmt::kAcc][4];
@@ -411,34 +413,32 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
         for (int i = 0; i < Fmt::kAcc; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll
         for (int q = 0; q < kMmaChunkBlocks; ++q) {
-            if (kFull || q < nb) {
-                const int col = Fmt::kGroupScale ? q : 0;
-                const uint4* bp = gq == col ? xs + (lb0 + q) * kBlk : zero;
-                const uint32_t ua[4] = {r.wa[q].x, r.wa[q].y, r.wa[q].z, r.wa[q].w};
-                const uint32_t ub[4] = {r.wb[q].x, r.wb[q].y, r.wb[q].z, r.wb[q].w};
-                if constexpr (Fmt::kGroupScale) {
+            const int col = Fmt::kGroupScale ? q : 0;
+            const uint4* bp = gq == col ? xs + (lb0 + q) * kBlk : zero;
+            const uint32_t ua[4] = {r.wa[q].x, r.wa[q].y, r.wa[q].z, r.wa[q].w};
+            const uint32_t ub[4] = {r.wb[q].x, r.wb[q].y, r.wb[q].z, r.wb[q].w};
+            if constexpr (Fmt::kGroupScale) {
 #pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        const uint4 bb = bp[w * 4 + t];  // (x0,x4) (x1,x5) (x2,x6) (x3,x7)
-                        const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
-                        mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ua[w]), nib_pair_lo(ub[w]),
-                                  nib_pair_hi(ua[w]), nib_pair_hi(ub[w]), bb.x, bb.y);
-                        mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ha), nib_pair_lo(hb),
-                                  nib_pair_hi(ha), nib_pair_hi(hb), bb.z, bb.w);
-                    }
-                } else {
+                for (int w = 0; w < 4; ++w) {
+                    const uint4 bb = bp[w * 4 + t];  // (x0,x4) (x1,x5) (x2,x6) (x3,x7)
+                    const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
+                    mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ua[w]), nib_pair_lo(ub[w]),
+                              nib_pair_hi(ua[w]), nib_pair_hi(ub[w]), bb.x, bb.y);
+                    mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ha), nib_pair_lo(hb),
+                              nib_pair_hi(ha), nib_pair_hi(hb), bb.z, bb.w);
+                }
+            } else {
 #pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        const uint4 bb = bp[2 * t + jj];  // x[16t + 8jj .. +8)
+                for (int jj = 0; jj < 2; ++jj) {
+                    const uint4 bb = bp[2 * t + jj];  // x[16t + 8jj .. +8)
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            __half2 qa[2], qb[2];
-                            int8x4_to_h2(ua[2 * jj + h], qa);
-                            int8x4_to_h2(ub[2 * jj + h], qb);
-                            mma_16816(acc[q % Fmt::kAcc], h2_as_u32(qa[0]), h2_as_u32(qb[0]),
-                                      h2_as_u32(qa[1]), h2_as_u32(qb[1]), h ? bb.z : bb.x,
-                                      h ? bb.w : bb.y);
-                        }
+                    for (int h = 0; h < 2; ++h) {
+                        __half2 qa[2], qb[2];
+                        int8x4_to_h2(ua[2 * jj + h], qa);
+                        int8x4_to_h2(ub[2 * jj + h], qb);
+                        mma_16816(acc[q % Fmt::kAcc], h2_as_u32(qa[0]), h2_as_u32(qb[0]),
+                                  h2_as_u32(qa[1]), h2_as_u32(qb[1]), h ? bb.z : bb.x,
+                                  h ? bb.w : bb.y);
                     }
                 }
             }
@@ -473,74 +473,62 @@ __device__ __forceinline__ void mma_item_t(const MmaItemRegs& r, const uint4* xs
         float (&out)[kNB][4] = sacc.v;
 #pragma unroll
         for (int q = 0; q < kMmaChunkBlocks; ++q) {
-            if (kFull || q < nb) {
-                const uint4* bq[kNB];
+            const uint4* bq[kNB];
 #pragma unroll
-                for (int j = 0; j < kNB; ++j) bq[j] = bp[j] ? bp[j] + (lb0 + q) * kBlk : zero;
-                const uint32_t ua[4] = {r.wa[q].x, r.wa[q].y, r.wa[q].z, r.wa[q].w};
-                const uint32_t ub[4] = {r.wb[q].x, r.wb[q].y, r.wb[q].z, r.wb[q].w};
-                if constexpr (Fmt::kGroupScale) {
-                    float bacc[kNB][4];
+            for (int j = 0; j < kNB; ++j) bq[j] = bp[j] ? bp[j] + (lb0 + q) * kBlk : zero;
+            const uint32_t ua[4] = {r.wa[q].x, r.wa[q].y, r.wa[q].z, r.wa[q].w};
+            const uint32_t ub[4] = {r.wb[q].x, r.wb[q].y, r.wb[q].z, r.wb[q].w};
+            if constexpr (Fmt::kGroupScale) {
+                float bacc[kNB][4];
+#pragma unroll
+                for (int j = 0; j < kNB; ++j)
+                    bacc[j][0] = bacc[j][1] = bacc[j][2] = bacc[j][3] = 0.f;
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    uint4 bb[kNB];
+#pragma unroll
+                    for (int j = 0; j < kNB; ++j) bb[j] = bq[j][w * 4 + t];
+                    const uint32_t a0 = nib_pair_lo(ua[w]), a1 = nib_pair_lo(ub[w]);
+                    const uint32_t a2 = nib_pair_hi(ua[w]), a3 = nib_pair_hi(ub[w]);
 #pragma unroll
                     for (int j = 0; j < kNB; ++j)
-                        bacc[j][0] = bacc[j][1] = bacc[j][2] = bacc[j][3] = 0.f;
+                        mma_16816(bacc[j], a0, a1, a2, a3, bb[j].x, bb[j].y);
+                    const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
+                    const uint32_t c0 = nib_pair_lo(ha), c1 = nib_pair_lo(hb);
+                    const uint32_t c2 = nib_pair_hi(ha), c3 = nib_pair_hi(hb);
 #pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        uint4 bb[kNB];
+                    for (int j = 0; j < kNB; ++j)
+                        mma_16816(bacc[j], c0, c1, c2, c3, bb[j].z, bb[j].w);
+                }
+                const float sa = scale_at(r.sa, q), sb = scale_at(r.sb, q);
 #pragma unroll
-                        for (int j = 0; j < kNB; ++j) bb[j] = bq[j][w * 4 + t];
-                        const uint32_t a0 = nib_pair_lo(ua[w]), a1 = nib_pair_lo(ub[w]);
-                        const uint32_t a2 = nib_pair_hi(ua[w]), a3 = nib_pair_hi(ub[w]);
+                for (int j = 0; j < kNB; ++j) {
+                    out[j][0] = fmaf(sa, bacc[j][0], out[j][0]);
+                    out[j][1] = fmaf(sa, bacc[j][1], out[j][1]);
+                    out[j][2] = fmaf(sb, bacc[j][2], out[j][2]);
+                    out[j][3] = fmaf(sb, bacc[j][3], out[j][3]);
+                }
+            } else {
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    uint4 bb[kNB];
+#pragma unroll
+                    for (int j = 0; j < kNB; ++j) bb[j] = bq[j][2 * t + jj];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        __half2 qa[2], qb[2];
+                        int8x4_to_h2(ua[2 * jj + h], qa);
+                        int8x4_to_h2(ub[2 * jj + h], qb);
 #pragma unroll
                         for (int j = 0; j < kNB; ++j)
-                            mma_16816(bacc[j], a0, a1, a2, a3, bb[j].x, bb[j].y);
-                        const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
-                        const uint32_t c0 = nib_pair_lo(ha), c1 = nib_pair_lo(hb);
-                        const uint32_t c2 = nib_pair_hi(ha), c3 = nib_pair_hi(hb);
-#pragma unroll
-                        for (int j = 0; j < kNB; ++j)
-                            mma_16816(bacc[j], c0, c1, c2, c3, bb[j].z, bb[j].w);
-                    }
-                    const float sa = scale_at(r.sa, q), sb = scale_at(r.sb, q);
-#pragma unroll
-                    for (int j = 0; j < kNB; ++j) {
-                        out[j][0] = fmaf(sa, bacc[j][0], out[j][0]);
-                        out[j][1] = fmaf(sa, bacc[j][1], out[j][1]);
-                        out[j][2] = fmaf(sb, bacc[j][2], out[j][2]);
-                        out[j][3] = fmaf(sb, bacc[j][3], out[j][3]);
-                    }
-                } else {
-#pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        uint4 bb[kNB];
-#pragma unroll
-                        for (int j = 0; j < kNB; ++j) bb[j] = bq[j][2 * t + jj];
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            __half2 qa[2], qb[2];
-                            int8x4_to_h2(ua[2 * jj + h], qa);
-                            int8x4_to_h2(ub[2 * jj + h], qb);
-#pragma unroll
-                            for (int j = 0; j < kNB; ++j)
-                                mma_16816(out[j], h2_as_u32(qa[0]), h2_as_u32(qb[0]),
-                                          h2_as_u32(qa[1]), h2_as_u32(qb[1]),
-                                          h ? bb[j].z : bb[j].x, h ? bb[j].w : bb[j].y);
-                        }
+                            mma_16816(out[j], h2_as_u32(qa[0]), h2_as_u32(qb[0]),
+                                      h2_as_u32(qa[1]), h2_as_u32(qb[1]),
+                                      h ? bb[j].z : bb[j].x, h ? bb[j].w : bb[j].y);
                     }
                 }
             }
         }
     }
-}
-
-template <class Fmt, int kNB, bool kAllFull>
-__device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, const uint4* zero,
-                                         int lb0, int blocks_left, const MmaGeom& g, int gq,
-                                         int t, MmaAcc<kNB>& sacc) {
-    if (kAllFull || blocks_left >= kMmaChunkBlocks)
-        mma_item_t<Fmt, kNB, true>(r, xs, zero, lb0, kMmaChunkBlocks, g, gq, t, sacc);
-    else
-        mma_item_t<Fmt, kNB, false>(r, xs, zero, lb0, blocks_left, g, gq, t, sacc);
 }
 
 // A warp's position: segment (tile, seg) and chunk j inside it.  Segments of
@@ -659,12 +647,14 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     // Without the caller's promise that x is not produced by the preceding
     // kernel, x may only be read after that kernel has completed.
     if (!g.early_x) pdl_wait_prior_grids();
-    // Activations of this split: INT4 in the permuted step order, INT8 as is.
-    // (row m, word q) pairs are walked in order, kStageBatch loads in flight
-    // per thread before their stores.
+    // Activations of this split: INT4 in the permuted step order, INT8 as is,
+    // zeros from the row end to the end of the last chunk.  (row m, word q)
+    // pairs are walked in order, kStageBatch loads in flight per thread before
+    // their stores.
     {
         constexpr int kStageBatch = 4;
-        const int words = lblocks * Fmt::kBlockWords;
+        const int valid = lblocks * Fmt::kBlockWords;
+        const int words = n_kc * kMmaChunkBlocks * Fmt::kBlockWords;
         const int64_t k_first = (int64_t)kMmaChunkBlocks * kc0 * Fmt::kBlockWords * 8;
         int m = 0, q = tid;
         while (m < M && q >= words) {
@@ -678,7 +668,8 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
             for (int u = 0; u < kStageBatch; ++u) {
                 ms[u] = m;
                 qs[u] = q;
-                if (m < M)
+                v[u] = make_uint4(0u, 0u, 0u, 0u);
+                if (m < M && q < valid)
                     v[u] = __ldg(reinterpret_cast<const uint4*>(x + m * g.x_stride + k_first) + q);
                 q += kThreads;
                 while (m < M && q >= words) {
@@ -778,7 +769,7 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
         if (rnd >= n_rounds) break;
         {
             const int lb0 = kMmaChunkBlocks * (ca.seg * G + ca.j);
-            mma_item<Fmt, kNB, kAllFull>(ra, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+            mma_item<Fmt, kNB>(ra, xs4, zero4, lb0, g, gq, t, sacc);
             if (seg_last(ca))
                 mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (ca.tile - rnd * RT) * n_seg + ca.seg);
         }
@@ -788,7 +779,7 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
         if (rnd >= n_rounds) break;
         {
             const int lb0 = kMmaChunkBlocks * (cb.seg * G + cb.j);
-            mma_item<Fmt, kNB, kAllFull>(rb, xs4, zero4, lb0, lblocks - lb0, g, gq, t, sacc);
+            mma_item<Fmt, kNB>(rb, xs4, zero4, lb0, g, gq, t, sacc);
             if (seg_last(cb))
                 mma_flush<Fmt, kNB>(sacc, g, gq, t, part, (cb.tile - rnd * RT) * n_seg + cb.seg);
         }
