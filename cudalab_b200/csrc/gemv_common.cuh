@@ -128,8 +128,10 @@ __device__ __forceinline__ void pdl_allow_dependents() {
 
 // System-scope release store / acquire load of a flag word that other GPUs
 // read or write through peer mappings.
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Strong (relaxed) system-scope store: after a fence.sc.sys it forms a
+// release pattern, without the implicit fence of st.release.
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;

@@ -194,9 +194,10 @@ struct PeerOut {
 // Called by thread 0 of every CTA after a CTA barrier that follows the CTA's
 // peer stores: the system-scope fence before the ticket publishes the whole
 // CTA's stores (cumulativity through the barrier); the last CTA's fence and
-// release stores publish every CTA's stores (through the ticket atomics).
-// Loops run over the compile-time peer slots so that `po` stays in the
-// parameter space (no local copy).
+// the strong stores after it (a release pattern: one fence for all peers, not
+// one per peer as st.release would imply) publish every CTA's stores (through
+// the ticket atomics).  Loops run over the compile-time peer slots so that
+// `po` stays in the parameter space (no local copy).
 __device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned epoch) {
     unsigned* mine = po.flag[po.rank];
     __threadfence_system();
@@ -206,7 +207,7 @@ __device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned
     __threadfence_system();
 #pragma unroll
     for (int p = 0; p < kMaxPeers; ++p)
-        if (p < po.world) st_release_sys(po.flag[p] + po.rank, epoch);
+        if (p < po.world) st_relaxed_sys(po.flag[p] + po.rank, epoch);
     const long long t0 = clock64();
     bool ok = true;
     for (int q = 0; q < po.world && ok; ++q) {
