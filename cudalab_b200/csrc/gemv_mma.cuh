@@ -34,7 +34,7 @@
 //
 // Batch columns
 //   * M = 1 (kNB = 0): INT4 block q of an item is fed through batch column q
-//     (the other lanes read a zero region), so one accumulator keeps the four
+//     (the other lanes read a zero region), so the accumulators keep the four
 //     groups apart and the group scales are applied once per item.  INT8 uses
 //     column 0 and applies the row scale at the very end.
 //   * M = 2..16 (kNB = 1 or 2 column blocks of 8): column c of block j is
@@ -308,7 +308,8 @@ __device__ __forceinline__ void mma_fetch(MmaItemRegs& r, const MmaFetchPtr& p,
 
 // Issue the loads of one item (tile, chunk kc of the split) in a matrix with a
 // short last chunk per row: blocks past the row end re-read the row's last
-// block (their mma is skipped).  Rows beyond the group re-read its last row.
+// block (the staged activations are zero there, so they add exact zeros).
+// Rows beyond the group re-read its last row.
 template <class Fmt, int kNB>
 __device__ __forceinline__ void mma_fetch_ragged(MmaItemRegs& r, const uint8_t* W,
                                                  const typename Fmt::Scale* scale,
