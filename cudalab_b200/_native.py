@@ -22,6 +22,9 @@ CL_LAUNCH_PDL = 1
 CL_LAUNCH_INPUTS_READY = 2
 CL_LAUNCH_OUTPUTS_FREE = 4
 
+CL_DTYPE_F16 = 0
+CL_DTYPE_F32 = 1
+
 CL_VARIANTS_NORMAL = 0
 CL_VARIANTS_ALL = 1
 CL_VARIANTS_QUARANTINED = 2
@@ -64,6 +67,11 @@ PROTOTYPES = {
     "cl_int4gemv_quantize": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "cl_qgemv_quantize": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "cl_qgemv_batched": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u32]),
+    "cl_gemv": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
+    "cl_gemv_ex": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _vp, _u32]),
+    "cl_gemv_native_timing": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _i64, _i64, _i64, _vp,
+                                     _u32, _dp]),
+    "cl_gemv_list_variants": (_int, [_int, ctypes.c_char_p, _size, ctypes.POINTER(_size)]),
 }
 
 CL_MAX_PEERS = 8
@@ -99,7 +107,8 @@ def last_error(lib=None) -> str:
 
 def list_variants(kind: str, which: int) -> list[str]:
     lib = load()
-    fn = lib.cl_int4gemv_list_variants if kind == "int4gemv" else lib.cl_qgemv_list_variants
+    fn = {"int4gemv": lib.cl_int4gemv_list_variants, "qgemv": lib.cl_qgemv_list_variants,
+          "gemv": lib.cl_gemv_list_variants}[kind]
     needed = _size(0)
     fn(which, None, 0, ctypes.byref(needed))
     buf = ctypes.create_string_buffer(max(1, needed.value))

@@ -33,7 +33,7 @@ HEADER = ROOT / "include" / "cudalab_gemv.h"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared"]
-SOURCES = ["gemv_kernels.cu", "quantize.cu", "capi.cu"]
+SOURCES = ["gemv_kernels.cu", "gemv_dense.cu", "quantize.cu", "capi.cu"]
 
 
 def _nvcc() -> str:
@@ -85,7 +85,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
 
 
 def build(op: str = "int4gemv", force: bool = False, verbose: bool = False):
-    """Return the extension object of operator `op` ("int4gemv" | "qgemv")."""
+    """Return the extension object of operator `op` ("int4gemv" | "qgemv" | "gemv")."""
     build_library(force=force, verbose=verbose)
     from .ext import get_ext
     return get_ext(op)

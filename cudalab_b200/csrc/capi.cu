@@ -73,7 +73,8 @@ int list_variants(const clb::VariantDesc* table, int n, int which, char* buf, si
     return CL_OK;
 }
 
-// Shared argument checks.  is_int4 adds the group-size contract K % 128 == 0.
+// Shared argument checks.  is_int4 adds the group-size contract K % 128 == 0;
+// `scale` may be null only for the dense GEMV (pass its W instead).
 int check_args(const char* op, const void* W, const void* scale, const void* x, const void* out,
                int64_t N, int64_t K, bool is_int4) {
     if (N <= 0) return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": N must be > 0");
@@ -315,6 +316,41 @@ int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed)
 }
 
 // ---- quantisation ----
+static const clb::VariantDesc* gemv_table(int dtype, int* n) {
+    if (dtype != CL_DTYPE_F16 && dtype != CL_DTYPE_F32) return nullptr;
+    return clb::gemv_variants(dtype, n);
+}
+
+int cl_gemv_ex(const char* variant, const void* W, const void* x, void* out, int64_t N, int64_t K,
+               int dtype, void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::VariantDesc* t = gemv_table(dtype, &n);
+    if (!t) return fail(CL_ERR_INVALID_ARGUMENT, "gemv: dtype must be CL_DTYPE_F16 or CL_DTYPE_F32");
+    return run(t, n, "gemv", variant, W, W, x, out, N, K, stream, flags, false);
+}
+
+int cl_gemv(const char* variant, const void* W, const void* x, void* out, int64_t N, int64_t K,
+            int dtype, void* stream) {
+    return cl_gemv_ex(variant, W, x, out, N, K, dtype, stream, 0u);
+}
+
+int cl_gemv_native_timing(const char* variant, const void* W, const void* x, void* out, int64_t N,
+                          int64_t K, int dtype, int64_t warmup, int64_t n_windows,
+                          int64_t launches_per_window, void* stream, uint32_t flags,
+                          double* per_window_us) {
+    int n = 0;
+    const clb::VariantDesc* t = gemv_table(dtype, &n);
+    if (!t) return fail(CL_ERR_INVALID_ARGUMENT, "gemv: dtype must be CL_DTYPE_F16 or CL_DTYPE_F32");
+    return timing(t, n, "gemv", variant, W, W, x, out, N, K, warmup, n_windows,
+                  launches_per_window, stream, flags, per_window_us, false);
+}
+
+int cl_gemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::gemv_variants(CL_DTYPE_F16, &n);  // same names for fp32
+    return list_variants(t, n, which, buf, buf_len, needed);
+}
+
 int cl_int4gemv_quantize(const void* W, int64_t N, int64_t K, uint8_t* W_packed, void* scale,
                          void* stream) {
     if (N <= 0 || K <= 0) return fail(CL_ERR_INVALID_ARGUMENT, "int4gemv_quantize: N, K must be > 0");

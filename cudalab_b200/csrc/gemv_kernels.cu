@@ -38,6 +38,9 @@ __global__ void __launch_bounds__(256) int4gemv_scalar_kernel(const uint8_t* __r
                                                               const __half* __restrict__ x,
                                                               __half* __restrict__ y, int64_t N,
                                                               int64_t K) {
+    // Under programmatic dependent launch the preceding kernel may still run:
+    // touch nothing before it has completed.
+    pdl_wait_prior_grids();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * 8 + warp;
     if (row >= N) return;
@@ -65,6 +68,7 @@ __global__ void __launch_bounds__(256) qgemv_scalar_kernel(const int8_t* __restr
                                                            const __half* __restrict__ x,
                                                            __half* __restrict__ y, int64_t N,
                                                            int64_t K) {
+    pdl_wait_prior_grids();  // as in int4gemv_scalar_kernel
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * 8 + warp;
     if (row >= N) return;
@@ -257,16 +261,18 @@ cudaError_t per_row(const GemvArgs& a, cudaStream_t s, unsigned flags) {
 //   CTAs, 2 for a shorter per-launch latency), capped by max_groups (clusters
 //   that can be resident at once).  Returns false when no split fits in
 //   shared memory.
-bool make_mma_geom(int64_t N, int64_t K, int64_t M, bool int4, int num_sms, int ctas_per_sm,
+bool make_mma_geom(int64_t N, int64_t K, int64_t M, int kind, int num_sms, int ctas_per_sm,
                    int64_t max_groups, MmaGeom& g) {
     g = MmaGeom{};
     g.N = N;
     g.K = K;
     g.M = (int32_t)M;
-    g.row_bytes = int4 ? K / 2 : K;
+    g.row_bytes = kind == MmaInt4::kKind ? K / 2 : kind == MmaInt8::kKind ? K : 2 * K;
     g.blocks = (int32_t)(g.row_bytes / 64);
     g.n_kc = (g.blocks + kMmaChunkBlocks - 1) / kMmaChunkBlocks;
-    const int bw = int4 ? MmaInt4::kBlockWords : MmaInt8::kBlockWords;
+    const int bw = kind == MmaInt4::kKind   ? MmaInt4::kBlockWords
+                   : kind == MmaInt8::kKind ? MmaInt8::kBlockWords
+                                            : MmaF16::kBlockWords;
     const int pad = M > 1 ? 4 : 0;  // 64 B between activation rows: no bank conflicts
     const int64_t tiles = (N + 15) / 16;
     const int64_t target = (int64_t)num_sms * ctas_per_sm;
@@ -341,16 +347,19 @@ template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer>
 cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, const PeerOut& po) {
     constexpr bool kInt4 = Fmt::kGroupScale;
     const bool ok = aligned16(a.W) && aligned16(a.x) && (a.x_stride % 8) == 0 &&
-                    (kInt4 ? (a.K % 128 == 0) : (a.K % 64 == 0)) && a.M >= 1 &&
+                    a.K % Fmt::kKAlign == 0 && a.M >= 1 &&
                     a.M <= kMmaMaxM;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     MmaGeom g;
-    const bool geom = ok && make_mma_geom(a.N, a.K, a.M, kInt4, sm_count(dev), kCtasPerSm, 0, g);
+    const bool geom =
+        ok && make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, 0, g);
     if (!geom) {
         if constexpr (kPeer) return ok ? cudaErrorInvalidConfiguration : cudaErrorMisalignedAddress;
-        return per_row<kInt4 ? launch_int4_scalar : launch_int8_scalar>(a, s, flags);
+        return per_row<Fmt::kKind == MmaInt4::kKind   ? launch_int4_scalar
+                       : Fmt::kKind == MmaInt8::kKind ? launch_int8_scalar
+                                                      : launch_f16_scalar>(a, s, flags);
     }
     g.x_stride = a.x_stride;
     g.y_stride = a.y_stride;
@@ -386,7 +395,8 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
             if (clusters < g.groups) {
                 const int64_t x_stride = g.x_stride, y_stride = g.y_stride;
                 const int early = g.early_x, free_y = g.free_y;
-                if (!make_mma_geom(a.N, a.K, a.M, kInt4, sm_count(dev), kCtasPerSm, clusters, g))
+                if (!make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, clusters,
+                                   g))
                     return cudaErrorInvalidConfiguration;
                 g.x_stride = x_stride;
                 g.y_stride = y_stride;
@@ -510,6 +520,10 @@ const VariantDesc kInt8Variants[] = {
 };
 
 }  // namespace
+
+cudaError_t launch_gemv_f16_mma(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    return launch_mma_auto<MmaF16>(a, s, flags);
+}
 
 const ShardedVariantDesc kInt4Sharded[] = {
     {"int4gemv_mma", launch_mma_sharded_auto<MmaInt4>},

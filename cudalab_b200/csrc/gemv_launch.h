@@ -8,8 +8,9 @@
 
 namespace clb {
 
-// One launch: W is uint8 [N, K/2] (INT4 packed) or int8 [N, K] (INT8); scale
-// is fp16 [N, K/128] (INT4) or fp32 [N] (INT8); x holds M activation rows of
+// One launch: W is uint8 [N, K/2] (INT4 packed), int8 [N, K] (INT8) or the
+// dense fp16 / fp32 [N, K]; scale is fp16 [N, K/128] (INT4), fp32 [N] (INT8)
+// or unused (dense); x holds M activation rows of
 // K halves (x_stride halves apart), y receives M rows of N halves (y_stride
 // apart; in peer mode, rows of the full matrix in every rank's buffer).
 struct GemvArgs {
@@ -52,6 +53,15 @@ const VariantDesc* int4_variants(int* count);
 const VariantDesc* int8_variants(int* count);
 const ShardedVariantDesc* int4_sharded_variants(int* count);
 const ShardedVariantDesc* int8_sharded_variants(int* count);
+
+// Dense GEMV (gemv_dense.cu): variant table by element type (0 = fp16,
+// 1 = fp32; GemvArgs.scale unused), the tensor-core fp16 launch
+// (gemv_kernels.cu) and the fp16 baseline launch, which is also the fallback
+// of the tensor-core path when its contract is not met.
+const VariantDesc* gemv_variants(int dtype, int* count);
+cudaError_t launch_gemv_f16_mma(const GemvArgs& args, cudaStream_t stream, unsigned flags);
+cudaError_t launch_f16_scalar(const void* W, const void* scale, const void* x, void* y, int64_t N,
+                              int64_t K, cudaStream_t stream, unsigned flags);
 
 // Reads (optionally clears) the device-side bounded-wait status word of the
 // current device.

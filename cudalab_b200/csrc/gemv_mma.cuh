@@ -1,6 +1,6 @@
 // Tensor-core weight-only GEMV / small-batch GEMM for sm_100a (INT4
-// group-scaled, INT8 row-scaled), Y[m, n] = sum_k (s * q[n, k]) * X[m, k] for
-// M = 1..16 activation rows.
+// group-scaled, INT8 row-scaled, and dense fp16 weights),
+// Y[m, n] = sum_k (s * q[n, k]) * X[m, k] for M = 1..16 activation rows.
 //
 // Why tensor cores at M = 1: on the CUDA cores the exact dequantisation plus
 // an fp32 multiply-add costs 4+ issued instructions per weight element
@@ -49,7 +49,8 @@
 // nibble pairs (0,4) and (1,5) of word w, step 2w+1 pairs (2,6) and (3,7) --
 // exactly what one lop3 yields -- and the activations are staged in shared
 // memory in that permuted order.  INT8: step j uses word j, byte pairs (0,1)
-// and (2,3), i.e. natural order.
+// and (2,3), i.e. natural order.  fp16: step s uses words 2s and 2s+1 (the
+// weights need no conversion), natural order too.
 #pragma once
 
 #include "gemv_common.cuh"
@@ -125,16 +126,38 @@ __device__ __forceinline__ uint32_t nib_pair_hi(uint32_t w) {
 // with the same column parity is exact (the other terms are zeros) and the
 // result does not depend on kAcc.
 struct MmaInt4 {
+    static constexpr int kKind = 0;  // layout id for the host geometry
+    static constexpr int kKAlign = 128;  // K multiple for whole 64-byte blocks / groups
     static constexpr bool kGroupScale = true;
+    static constexpr bool kRowScale = false;
+    static constexpr bool kDense = false;
     static constexpr int kBlockWords = 16;  // 16-byte words of activations per block
     static constexpr int kAcc = 4;
     using Scale = __half;
 };
 struct MmaInt8 {
+    static constexpr int kKind = 1;  // layout id for the host geometry
+    static constexpr int kKAlign = 64;  // K multiple for whole 64-byte blocks / groups
     static constexpr bool kGroupScale = false;
+    static constexpr bool kRowScale = true;
+    static constexpr bool kDense = false;
     static constexpr int kBlockWords = 8;
     static constexpr int kAcc = 2;
     using Scale = float;
+};
+// Dense fp16 weights (no scale): a 64-byte block is 32 halves, lane t of a
+// quad holds halves 8t .. 8t+7 of its rows, and mma step s takes halves
+// 4s .. 4s+3 as k-slots (2t, 2t+1, 2t+8, 2t+9), so the activations keep
+// their natural order.
+struct MmaF16 {
+    static constexpr int kKind = 2;  // layout id for the host geometry
+    static constexpr int kKAlign = 32;  // K multiple for whole 64-byte blocks / groups
+    static constexpr bool kGroupScale = false;
+    static constexpr bool kRowScale = false;
+    static constexpr bool kDense = true;
+    static constexpr int kBlockWords = 4;
+    static constexpr int kAcc = 2;
+    using Scale = float;  // unused
 };
 
 // ---- cluster helpers (splits > 1) ----
@@ -429,6 +452,10 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
                     mma_16816(acc[q % Fmt::kAcc], nib_pair_lo(ha), nib_pair_lo(hb),
                               nib_pair_hi(ha), nib_pair_hi(hb), bb.z, bb.w);
                 }
+            } else if constexpr (Fmt::kDense) {
+                const uint4 bb = bp[t];  // x[8t .. 8t + 8) of the block
+                mma_16816(acc[q % Fmt::kAcc], ua[0], ub[0], ua[1], ub[1], bb.x, bb.y);
+                mma_16816(acc[q % Fmt::kAcc], ua[2], ub[2], ua[3], ub[3], bb.z, bb.w);
             } else {
 #pragma unroll
                 for (int jj = 0; jj < 2; ++jj) {
@@ -462,7 +489,7 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
             sacc.v[0][0] += fmaf(sa1, e1, sa0 * e0);
             sacc.v[0][1] += fmaf(sb1, e3, sb0 * e2);
         } else {
-            static_assert(Fmt::kAcc == 2, "INT8 sums its two accumulators");
+            static_assert(Fmt::kAcc == 2, "INT8 / fp16 sum their two accumulators");
             sacc.v[0][0] += acc[0][0] + acc[1][0];
             sacc.v[0][1] += acc[0][2] + acc[1][2];
         }
@@ -509,6 +536,15 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
                     out[j][1] = fmaf(sa, bacc[j][1], out[j][1]);
                     out[j][2] = fmaf(sb, bacc[j][2], out[j][2]);
                     out[j][3] = fmaf(sb, bacc[j][3], out[j][3]);
+                }
+            } else if constexpr (Fmt::kDense) {
+                uint4 bb[kNB];
+#pragma unroll
+                for (int j = 0; j < kNB; ++j) bb[j] = bq[j][t];
+#pragma unroll
+                for (int j = 0; j < kNB; ++j) {
+                    mma_16816(out[j], ua[0], ub[0], ua[1], ub[1], bb[j].x, bb[j].y);
+                    mma_16816(out[j], ua[2], ub[2], ua[3], ub[3], bb[j].z, bb[j].w);
                 }
             } else {
 #pragma unroll
@@ -640,7 +676,7 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     if (f.tile < n_tiles) fetch_next(ra);
     MmaSegCursor cb = f;
     if (f.tile < n_tiles) fetch_next(rb);
-    if constexpr (!Fmt::kGroupScale) {
+    if constexpr (Fmt::kRowScale) {
         for (int r = tid; r < nrows; r += kThreads)
             sc8[r] = reinterpret_cast<const float*>(scale)[r0 + r];
     }
@@ -749,7 +785,7 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
                 float s = 0.f;
                 for (int sg = 0; sg < n_seg; ++sg) s += pp[sg * 16 * M];
                 if (g.splits == 1) {
-                    if constexpr (!Fmt::kGroupScale) s *= sc8[r];
+                    if constexpr (Fmt::kRowScale) s *= sc8[r];
                     store(r, m, s);
                 } else {
                     rsum[r * M + m] = s;
@@ -800,7 +836,7 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
             for (int r = lo + tid; r < hi; r += kThreads) {
                 float s = 0.f;
                 for (int sp = 0; sp < g.splits; ++sp) s += ld_cluster_f32(rsum + r * M + m, sp);
-                if constexpr (!Fmt::kGroupScale) s *= sc8[r];
+                if constexpr (Fmt::kRowScale) s *= sc8[r];
                 store(r, m, s);
             }
         }

@@ -14,7 +14,8 @@ point is the median of `--blocks` such timings.  One JSON line per point:
 
 `flags` are the C-ABI launch flags (1 = programmatic dependent launch,
 3 = x not produced by the preceding kernel, 7 = neither is y).  GB/s counts
-the algorithmic bytes of one GEMV (weights, scales, x, y).
+the algorithmic bytes of one GEMV (weights, scales, x, y).  Kinds: int4gemv,
+qgemv, gemv (dense fp16) and gemv_f32 (dense fp32; M = 1 only).
 """
 from __future__ import annotations
 
@@ -28,6 +29,7 @@ import torch
 from cudalab_b200 import _native as nat
 from cudalab_b200.build import build
 from cudalab_b200.int4gemv_quantize import quantize_w as quantize_int4
+from cudalab_b200.operators.gemv import algorithmic_bytes_gemv, make_w
 from cudalab_b200.operators.int4gemv import algorithmic_bytes_int4
 from cudalab_b200.operators.qgemv import algorithmic_bytes_int8
 from cudalab_b200.qgemv_quantize import quantize_w as quantize_int8
@@ -45,9 +47,14 @@ def measured_hbm_gbs() -> float | None:
 
 
 def weight_pool(kind: str, N: int, K: int, pool: int) -> list:
-    quant = quantize_int4 if kind == "int4gemv" else quantize_int8
+    """(weights, scales) per pool entry; scales are None for the dense GEMV."""
     out = []
     for i in range(pool):
+        if kind in ("gemv", "gemv_f32"):
+            dt = torch.float16 if kind == "gemv" else torch.float32
+            out.append((make_w(N, K, dt, device="cuda", seed=1000 + i, scale=0.02), None))
+            continue
+        quant = quantize_int4 if kind == "int4gemv" else quantize_int8
         g = torch.Generator().manual_seed(1000 + i)
         W = (torch.randn(N, K, generator=g) * 0.02).half().cuda()
         out.append(quant(W))
@@ -65,7 +72,9 @@ def time_point(ext, variant: str, ws: list, X: torch.Tensor, Y: torch.Tensor, fl
     def body():
         for i in range(launches):
             w, sc = ws[i % len(ws)]
-            if M == 1:
+            if sc is None:
+                ext.forward_into(variant, w, X[0], Y[0], flags=flags)
+            elif M == 1:
                 ext.forward_into(variant, w, sc, X[0], Y[0], flags=flags)
             else:
                 ext.forward_batched_into(variant, w, sc, X, Y, flags=flags)
@@ -108,18 +117,25 @@ def main(argv=None) -> int:
     if not torch.cuda.is_available():
         raise SystemExit("sweep needs a CUDA device")
     peak = measured_hbm_gbs()
-    exts = {k: build(k) for k in args.kinds.split(",")}
+    exts = {k: build("gemv" if k == "gemv_f32" else k) for k in args.kinds.split(",")}
     for kind, ext in exts.items():
-        variant = f"{kind}_{args.variant}"
-        bytes_fn = algorithmic_bytes_int4 if kind == "int4gemv" else algorithmic_bytes_int8
+        variant = f"{'gemv' if kind == 'gemv_f32' else kind}_{args.variant}"
+        es = 4 if kind == "gemv_f32" else 2
+        bytes_fn = {"int4gemv": algorithmic_bytes_int4, "qgemv": algorithmic_bytes_int8,
+                    "gemv": lambda N, K, M: algorithmic_bytes_gemv(N, K, es) if M else N * K * es,
+                    "gemv_f32": lambda N, K, M: algorithmic_bytes_gemv(N, K, es) if M
+                    else N * K * es}[kind]
         for shape in args.shapes.split(","):
             N, K = (int(v) for v in shape.lower().split("x"))
             wbytes = bytes_fn(N, K, 0)
             pool = args.pool or max(2, -(-3 * L2_BYTES // wbytes))
             ws = weight_pool(kind, N, K, pool)
+            xdt = torch.float32 if kind == "gemv_f32" else torch.float16
             for M in (int(m) for m in args.batches.split(",")):
-                X = torch.randn(M, K, generator=torch.Generator().manual_seed(7)).half().cuda()
-                Y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+                if kind.startswith("gemv") and M != 1:
+                    continue
+                X = torch.randn(M, K, generator=torch.Generator().manual_seed(7)).to(xdt).cuda()
+                Y = torch.empty(M, N, device="cuda", dtype=xdt)
                 torch.cuda.synchronize()
                 for flags in (int(f) for f in args.flags.split(",")):
                     us = time_point(ext, variant, ws, X, Y, flags, args.launches, args.reps,

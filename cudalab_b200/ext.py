@@ -3,7 +3,8 @@ per-operator pybind modules.
 
 `Int4gemvExt` mirrors kernels/int4gemv/bindings.cpp (forward :145-159,
 forward_into :163-176, native_timing :180-253, variant lists :258-285) and
-`QgemvExt` mirrors kernels/qgemv/bindings.cpp (:66-115, :281-306).  The
+`QgemvExt` mirrors kernels/qgemv/bindings.cpp (:66-115, :281-306), `GemvExt`
+kernels/gemv/bindings.cpp (dense fp16 / fp32 GEMV).  The
 tensor-metadata checks run here, before any device work, in the reference's
 order (variant lookup, then W: dim -> N>0 -> K>0 -> dtype -> [K%128] ->
 contiguous -> is_cuda, then scale, x, out), and raise RuntimeError whose first
@@ -281,10 +282,143 @@ class QgemvExt(_ExtBase):
 _EXTS: dict = {}
 
 
+class GemvExt:
+    """Dense GEMV, y = W @ x with W fp16 / fp32 [N, K], x [K], y [N] of the
+    same dtype, fp32 accumulation: mirrors kernels/gemv/bindings.cpp (checks
+    :86-125 in that order, forward :136-162, forward_into :166-191,
+    native_timing :195-266, variant lists :271-306), each message's first
+    part the reference's text, then an English rendering."""
+    kind = "gemv"
+
+    def __init__(self) -> None:
+        self._lib = nat.load()
+        self._cache = {}
+
+    def variants(self) -> list[str]:
+        return nat.list_variants("gemv", nat.CL_VARIANTS_NORMAL)
+
+    def all_variants(self) -> list[str]:
+        return nat.list_variants("gemv", nat.CL_VARIANTS_ALL)
+
+    def quarantined_variants(self) -> list[str]:
+        return nat.list_variants("gemv", nat.CL_VARIANTS_QUARANTINED)
+
+    def _check_variant(self, name: str) -> None:
+        allv = self._cache.get("all")
+        if allv is None:
+            allv = self._cache["all"] = set(self.all_variants())
+        if name not in allv:
+            normal = " ".join(self.variants())
+            quarantined = " ".join(self.quarantined_variants())
+            raise RuntimeError(f"未知 gemv 变体 '{name}'。正常可用: {normal} "
+                               f"；被隔离（NOT_FOR_NORMAL_DISPATCH）: {quarantined} "
+                               "（显式命名仍可调用，属受控历史审计入口） (unknown gemv variant)")
+
+    @staticmethod
+    def _validate_w(W: torch.Tensor) -> None:
+        _chk(W.dim() == 2, f"W 必须是 2 维 (N, K)，实际 {W.dim()} 维 (W must be 2-D)")
+        _chk(W.size(0) > 0, f"N 必须 > 0，实际 {W.size(0)} (N must be > 0)")
+        _chk(W.size(1) > 0, f"K 必须 > 0，实际 {W.size(1)} (K must be > 0)")
+        _chk(W.dtype in (torch.float16, torch.float32),
+             f"仅支持 float16 / float32，实际 {W.dtype} (only float16 / float32)")
+        _chk(W.is_contiguous(), "W 必须是连续内存 (W must be contiguous)")
+        _chk(W.is_cuda, "W 必须是 CUDA 张量 (W must be a CUDA tensor)")
+
+    @staticmethod
+    def _validate_x(W: torch.Tensor, x: torch.Tensor) -> None:
+        _chk(x.dim() == 1, f"x 必须是 1 维 (K,)，实际 {x.dim()} 维 (x must be 1-D)")
+        _chk(x.size(0) == W.size(1),
+             f"x 长度必须等于 K: x={x.size(0)} K={W.size(1)} (len(x) must equal K)")
+        _chk(x.dtype == W.dtype,
+             f"x 的 dtype 必须与 W 一致: x={x.dtype} W={W.dtype} (x dtype must equal W dtype)")
+        _chk(x.is_contiguous(), "x 必须是连续内存 (x must be contiguous)")
+        _chk(x.is_cuda, "x 必须是 CUDA 张量 (x must be a CUDA tensor)")
+        _chk(x.device == W.device, "x 必须与 W 在同一 CUDA 设备上 (x must be on the device of W)")
+
+    @staticmethod
+    def _validate_out(W: torch.Tensor, out: torch.Tensor) -> None:
+        _chk(out.dim() == 1, f"out 必须是 1 维 (N,)，实际 {out.dim()} 维 (out must be 1-D)")
+        _chk(out.size(0) == W.size(0),
+             f"out 长度必须等于 N: out={out.size(0)} N={W.size(0)} (len(out) must equal N)")
+        _chk(out.dtype == W.dtype,
+             f"out 的 dtype 必须与 W 一致: out={out.dtype} W={W.dtype} "
+             "(out dtype must equal W dtype)")
+        _chk(out.is_contiguous(), "out 必须是连续内存 (out must be contiguous)")
+        _chk(out.is_cuda, "out 必须是 CUDA 张量 (out must be a CUDA tensor)")
+        _chk(out.device == W.device,
+             "out 必须与 W 在同一 CUDA 设备上 (out must be on the device of W)")
+
+    @staticmethod
+    def _dtype_code(W: torch.Tensor) -> int:
+        return nat.CL_DTYPE_F16 if W.dtype == torch.float16 else nat.CL_DTYPE_F32
+
+    def _launch(self, name: str, W, x, out, flags: int = 0) -> None:
+        dev = W.device
+        with torch.cuda.device(dev):
+            rc = self._lib.cl_gemv_ex(name.encode(), W.data_ptr(), x.data_ptr(), out.data_ptr(),
+                                      W.size(0), W.size(1), self._dtype_code(W), _stream_ptr(dev),
+                                      flags)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"gemv launch failed ({rc}): {nat.last_error(self._lib)}")
+
+    def forward(self, variant: str, W, x, flags: int = 0) -> torch.Tensor:
+        self._check_variant(variant)
+        self._validate_w(W)
+        self._validate_x(W, x)
+        out = torch.empty(W.size(0), dtype=W.dtype, device=W.device)
+        self._launch(variant, W, x, out, flags)
+        return out
+
+    def forward_into(self, variant: str, W, x, out, flags: int = 0) -> None:
+        self._check_variant(variant)
+        self._validate_w(W)
+        self._validate_x(W, x)
+        self._validate_out(W, out)
+        self._launch(variant, W, x, out, flags)
+
+    def native_timing(self, variant: str, W, x, out, warmup: int = 200, n_windows: int = 10,
+                      launches_per_window: int = 64, flags: int = 0) -> dict:
+        self._check_variant(variant)
+        _chk(warmup >= 0, f"warmup 必须 >= 0，实际 {warmup} (warmup must be >= 0)")
+        _chk(n_windows >= 1, f"n_windows 必须 >= 1，实际 {n_windows} (n_windows must be >= 1)")
+        _chk(launches_per_window >= 1,
+             f"launches_per_window 必须 >= 1，实际 {launches_per_window} "
+             "(launches_per_window must be >= 1)")
+        self._validate_w(W)
+        self._validate_x(W, x)
+        self._validate_out(W, out)
+        buf = (ctypes.c_double * n_windows)()
+        dev = W.device
+        with torch.cuda.device(dev):
+            rc = self._lib.cl_gemv_native_timing(
+                variant.encode(), W.data_ptr(), x.data_ptr(), out.data_ptr(), W.size(0),
+                W.size(1), self._dtype_code(W), warmup, n_windows, launches_per_window,
+                _stream_ptr(dev), flags, buf)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"native_timing failed ({rc}): {nat.last_error(self._lib)}")
+        per = [float(v) for v in buf]
+        s = sorted(per)
+        return {
+            "variant": variant,
+            "warmup": warmup,
+            "n_windows": n_windows,
+            "launches_per_window": launches_per_window,
+            "window_median_us": per,
+            "median_us": statistics.median(s),
+            "min_us": s[0],
+            "max_us": s[-1],
+            "mean_us": sum(s) / len(s),
+            "note": NATIVE_NOTE,
+        }
+
+
+_EXT_TYPES = {"int4gemv": Int4gemvExt, "qgemv": QgemvExt, "gemv": GemvExt}
+
+
 def get_ext(op: str):
     """Singleton extension object for `op`."""
-    if op not in ("int4gemv", "qgemv"):
-        raise RuntimeError(f"unknown operator {op!r}; available: int4gemv, qgemv")
+    if op not in _EXT_TYPES:
+        raise RuntimeError(f"unknown operator {op!r}; available: {', '.join(_EXT_TYPES)}")
     if op not in _EXTS:
-        _EXTS[op] = Int4gemvExt() if op == "int4gemv" else QgemvExt()
+        _EXTS[op] = _EXT_TYPES[op]()
     return _EXTS[op]

@@ -65,3 +65,27 @@ def make_x(K: int, dtype: torch.dtype = torch.float16, device: str = "cpu", seed
     else:
         raise ValueError(f"unknown input mode: {mode}")
     return x.to(dtype).contiguous().to(device)
+
+
+# ---- the dense GEMV operator itself (cudalab/operators/gemv.py:192-201,
+#      :283-289 of the reference) ----
+
+# LLM hidden / MLP projection shapes (N, K) of the reference's bench matrix.
+BENCH_MATRIX_GEMV = ((1024, 4096), (4096, 1024), (4096, 4096), (11008, 4096), (4096, 11008))
+PRIMARY_TARGET = (4096, 4096)
+
+
+def gemv_ref(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """Reference result: fp16 -> fp16(mv(W.float(), x.float())); fp32 -> mv(W, x)."""
+    if W.dim() != 2:
+        raise ValueError(f"expected a 2-D W (N, K), got {W.dim()}-D")
+    if x.dim() != 1:
+        raise ValueError(f"expected a 1-D x (K,), got {x.dim()}-D")
+    if W.dtype == torch.float16:
+        return torch.mv(W.float(), x.float()).to(torch.float16)
+    return torch.mv(W, x)
+
+
+def algorithmic_bytes_gemv(N: int, K: int, element_size: int = 2) -> int:
+    """W read + x read + y write: (N*K + K + N) * element_size."""
+    return (N * K + K + N) * element_size

@@ -142,6 +142,30 @@ int cl_qgemv_native_timing(const char* variant, const int8_t* W_q, const float* 
  * kernels/qgemv/bindings.cpp:281-306. */
 int cl_qgemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
 
+/* ---- dense GEMV (fp16 or fp32 weights and activations) ----
+ * y[n] = sum_k W[n, k] * x[k], fp32 accumulation, one rounding to the
+ * element type at the end; W [N, K] row-major, x [K], y [N], all of element
+ * type `dtype` (CL_DTYPE_F16 / CL_DTYPE_F32).  Replace `forward` /
+ * `forward_into` / `native_timing` / the variant lists of
+ * kernels/gemv/bindings.cpp:136-336 (tensor-level checks of
+ * bindings.cpp:86-125 are made by the host wrapper).  Variants: gemv_baseline,
+ * gemv_vec4_row, gemv_warp_vec4, gemv_splitk4 (quarantined, as in the
+ * reference), gemv_mma (fp16: tensor cores; fp32: CUDA cores).  A vectorised
+ * variant whose alignment contract is not met (W or x not 16-byte aligned, K
+ * not a multiple of the elements per 16 bytes; gemv_mma fp16: of 32) runs the
+ * baseline kernel and returns its bits. */
+#define CL_DTYPE_F16 0
+#define CL_DTYPE_F32 1
+int cl_gemv_ex(const char* variant, const void* W, const void* x, void* out, int64_t N, int64_t K,
+               int dtype, void* stream, uint32_t flags);
+int cl_gemv(const char* variant, const void* W, const void* x, void* out, int64_t N, int64_t K,
+            int dtype, void* stream);
+int cl_gemv_native_timing(const char* variant, const void* W, const void* x, void* out, int64_t N,
+                          int64_t K, int dtype, int64_t warmup, int64_t n_windows,
+                          int64_t launches_per_window, void* stream, uint32_t flags,
+                          double* per_window_us);
+int cl_gemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
+
 /* ---- quantisation on the device ----
  * Replace the offline torch quantisers quantize_w of
  * cudalab/int4gemv_quantize.py:61-114 (INT4: group 128, scale fp16 =

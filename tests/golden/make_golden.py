@@ -5,10 +5,13 @@ Runs ONLY in the build container, where the reference tree is mounted
 reference's own CPU code -- its generators (cudalab/operators/gemv.py:
 make_w/make_x), quantisers (cudalab/int4gemv_quantize.py,
 cudalab/qgemv_quantize.py), layer-A references and fp64 exact values -- and
-stores inputs and outputs as small .npz fixtures next to this script.  The
+stores inputs and outputs as small .npz fixtures next to this script (the
+dense GEMV fixture: the reference's gemv_ref and gate,
+cudalab/operators/gemv.py:192-201, cudalab/gemv_correctness.py:163-191).  The
 fixtures travel; the reference does not.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py               # all fixtures
+    python tests/golden/make_golden.py --only-gemv   # the dense GEMV fixture
 """
 from __future__ import annotations
 
@@ -31,6 +34,19 @@ INT4_CASES = [  # (N, K, mode, seed_w, seed_x)
     (32, 2048, "normal", 6, 7),
     (5, 384, "normal", 8, 9),
 ]
+GEMV_CASES = [  # (dtype, N, K, mode, seed_w, seed_x)
+    ("float16", 8, 64, "normal", 0, 1),
+    ("float16", 16, 13, "mixed_sign", 0, 1),
+    ("float16", 4, 4096, "large", 2, 3),
+    ("float16", 5, 7, "tiny", 4, 5),
+    ("float16", 2, 16, "zeros", 0, 1),
+    ("float16", 32, 1024, "normal", 6, 7),
+    ("float32", 8, 64, "normal", 0, 1),
+    ("float32", 16, 13, "mixed_sign", 0, 1),
+    ("float32", 3, 4096, "large", 2, 3),
+    ("float32", 64, 1, "normal", 4, 5),
+    ("float32", 32, 1024, "tiny", 6, 7),
+]
 INT8_CASES = [
     (8, 64, "normal", 0, 1),
     (16, 13, "mixed_sign", 0, 1),
@@ -46,10 +62,52 @@ def _bits16(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
 
 
+def _raw(t: torch.Tensor) -> np.ndarray:
+    """Element bits of an fp16 / fp32 tensor."""
+    if t.dtype == torch.float16:
+        return _bits16(t)
+    return t.contiguous().view(torch.int32).numpy().view(np.uint32).copy()
+
+
+def make_gemv() -> None:
+    """Dense GEMV fixtures: the reference's generators, gemv_ref and gate."""
+    from cudalab.operators.gemv import make_w, make_x, gemv_ref  # reference code
+    from cudalab.gemv_correctness import arith_ratio
+
+    out = {}
+    for i, (dt, N, K, mode, sw, sx) in enumerate(GEMV_CASES):
+        dtype = getattr(torch, dt)
+        W = make_w(N, K, dtype, device="cpu", seed=sw, mode=mode, large=10.0)
+        x = make_x(K, dtype, device="cpu", seed=sx, mode=mode, large=10.0)
+        y_ref = gemv_ref(W, x)
+        exact = torch.mv(W.double(), x.double())
+        S = (W.double().abs() * x.double().abs().unsqueeze(0)).sum(dim=1)
+        ratio, _, _ = arith_ratio(y_ref, W, x, dt)
+        p = f"c{i}_"
+        out[p + "meta"] = np.array([N, K, sw, sx], np.int64)
+        out[p + "dtype"] = np.array(dt)
+        out[p + "mode"] = np.array(mode)
+        out[p + "W"] = _raw(W)
+        out[p + "x"] = _raw(x)
+        out[p + "y_ref"] = _raw(y_ref)
+        out[p + "exact"] = exact.numpy()
+        out[p + "S"] = S.numpy()
+        out[p + "ref_ratio"] = np.array(ratio)
+    out["n_cases"] = np.array(len(GEMV_CASES))
+    np.savez_compressed(HERE / "gemv_golden.npz", **out)
+    print("wrote", HERE / "gemv_golden.npz")
+
+
 def main() -> None:
     if not REF.exists():
         raise SystemExit(f"reference tree not found at {REF}; fixtures are committed already")
     sys.path.insert(0, str(REF))
+    if "--only-gemv" not in sys.argv:
+        make_quantized()
+    make_gemv()
+
+
+def make_quantized() -> None:
     from cudalab.operators.gemv import make_w, make_x  # reference generators
     from cudalab import int4gemv_quantize as q4
     from cudalab import qgemv_quantize as q8
