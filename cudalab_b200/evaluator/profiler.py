@@ -6,10 +6,10 @@ parses the per-launch metrics into a summary.  Always passes
 kernel (`-k`), a handful of launches (`-c`).  Adds the metrics the reference's
 list lacked: dram__bytes_read.sum / dram__bytes_write.sum (physical DRAM
 traffic per launch, compared against the algorithmic bytes) and the tensor /
-issue counters used to judge instruction-boundness.
+issue counters that tell whether a kernel is bound by instruction issue.
 
     python -m cudalab_b200.evaluator.profiler --op int4gemv --variant int4gemv_bulk \
-        --N 4096 --K 4096 --out gpurun_out/prof_int4_bulk.json
+        --N 4096 --K 4096 --out prof_int4_bulk.json
 """
 from __future__ import annotations
 

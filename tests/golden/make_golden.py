@@ -1,7 +1,8 @@
 """Generate the golden vectors that pin the oracle and the product quantisers.
 
 Runs ONLY in the build container, where the reference tree is mounted
-(default /root/reference, override with CUDALAB_REFERENCE).  It imports the
+beside the repository (directory `reference` next to the repository root;
+override with CUDALAB_REFERENCE).  It imports the
 reference's own CPU code -- its generators (cudalab/operators/gemv.py:
 make_w/make_x), quantisers (cudalab/int4gemv_quantize.py,
 cudalab/qgemv_quantize.py), layer-A references and fp64 exact values -- and
@@ -23,7 +24,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("CUDALAB_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("CUDALAB_REFERENCE", HERE.parents[2] / "reference"))
 
 INT4_CASES = [  # (N, K, mode, seed_w, seed_x)
     (8, 128, "normal", 0, 1),
