@@ -18,7 +18,8 @@
 //   gemv_mma        fp16: the tensor-core kernel of gemv_mma.cuh with dense
 //                   weights (exact fp16 products, fp32 accumulation);
 //                   fp32: one warp per row with eight 16-byte loads in flight
-//                   per lane (tensor cores would round fp32 operands to tf32).
+//                   per lane, or one CTA per row for a few long rows (tensor
+//                   cores would round fp32 operands to tf32).
 // Vectorised contract: W and x 16-byte aligned and K a multiple of the
 // elements per 16 bytes (gemv_mma fp16: K a multiple of 32); otherwise the
 // baseline kernel runs.  Every kernel waits for the preceding grid before it
@@ -216,6 +217,15 @@ cudaError_t run_splitk4(const GemvArgs& a, cudaStream_t s, unsigned flags) {
                       static_cast<T*>(a.y), a.K);
 }
 
+// fp32 production path: one warp per row with eight loads in flight, except
+// for few long rows (N <= 2048, K >= 2048), where a warp per row leaves most
+// of the GPU idle and a whole CTA per row streams them (measured on B200:
+// 1024 x 4096 in 4.75 instead of 9.17 us).
+cudaError_t run_f32_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    if (a.N <= 2048 && a.K >= 2048) return run_vec_row<float>(a, s, flags);
+    return run_warp<float, 8>(a, s, flags);
+}
+
 const VariantDesc kF16Variants[] = {
     {"gemv_baseline", run_scalar<__half>, false},
     {"gemv_mma", launch_gemv_f16_mma, false},
@@ -226,7 +236,7 @@ const VariantDesc kF16Variants[] = {
 
 const VariantDesc kF32Variants[] = {
     {"gemv_baseline", run_scalar<float>, false},
-    {"gemv_mma", run_warp<float, 8>, false},
+    {"gemv_mma", run_f32_auto, false},
     {"gemv_splitk4", run_splitk4<float>, true},
     {"gemv_vec4_row", run_vec_row<float>, false},
     {"gemv_warp_vec4", run_warp<float, 1>, false},
