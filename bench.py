@@ -379,6 +379,27 @@ def main():
     g8 = capture(pool8, ext8, args.int8_variant, flags)
     us8 = replay_us(g8, args.context_reps)
     del g8, pool8
+    # The dense fp16 GEMV operator on the same shape: 16 weight matrices
+    # (537 MB > L2) cycled, same flags (context line)
+    from cudalab_b200.operators.gemv import algorithmic_bytes_gemv
+
+    class _DensePool:
+        def __init__(self, n):
+            gen = torch.Generator(device="cuda")
+            gen.manual_seed(4321)
+            self.ws = [(torch.randn(N_ROWS, K_COLS, generator=gen, device="cuda") * 0.02).half()
+                       for _ in range(n)]
+            self.x = torch.randn(K_COLS, generator=gen, device="cuda").half()
+            self.y = torch.empty(N_ROWS, dtype=torch.float16, device="cuda")
+
+        def launch(self, e, variant, i, flags=0):
+            e.forward_into(variant, self.ws[i % len(self.ws)], self.x, self.y, flags=flags)
+
+    extd = build("gemv")
+    poold = _DensePool(16)
+    gd = capture(poold, extd, "gemv_mma", flags)
+    usd = replay_us(gd, args.context_reps)
+    del gd, poold
     # The reference's own "streaming" pool (x and y rotate, one weight set, so
     # on B200 the 8.7 MB of weights stay in L2): context only, the headline
     # rotates 64 weight sets through HBM
@@ -431,6 +452,11 @@ def main():
             "int8": {"variant": args.int8_variant, "us_per_gemv": round(us8, 4),
                      "gbs": round(algorithmic_bytes_int8(N_ROWS, K_COLS) / (us8 * 1e-6) / 1e9, 1),
                      "int4_over_int8_speedup": round(us8 / us_per_gemv, 3)},
+            "gemv_fp16": {"variant": "gemv_mma", "us_per_gemv": round(usd, 4),
+                          "gbs": round(algorithmic_bytes_gemv(N_ROWS, K_COLS, 2) / (usd * 1e-6)
+                                       / 1e9, 1),
+                          "frac_of_peak": round(algorithmic_bytes_gemv(N_ROWS, K_COLS, 2)
+                                                / (usd * 1e-6) / 1e9 / peak, 4)},
             "gpu_launches": launches,
             "device_status": status,
             "clocks": sampler.summary(),
