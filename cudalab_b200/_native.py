@@ -67,6 +67,7 @@ PROTOTYPES = {
     "cl_int4gemv_quantize": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "cl_qgemv_quantize": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "cl_qgemv_batched": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u32]),
+    "cl_int4gemv_fused_noalloc": (_int, [_cs, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _u32]),
     "cl_gemv": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "cl_gemv_ex": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _vp, _u32]),
     "cl_gemv_native_timing": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _i64, _i64, _i64, _vp,

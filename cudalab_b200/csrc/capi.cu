@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -226,6 +227,44 @@ int run_sharded(const clb::ShardedVariantDesc* table, int n, const char* op, con
     return CL_OK;
 }
 
+// ---- the fused single-GPU step without an allocated flag block ----
+//
+// Scratch of cl_int4gemv_fused_noalloc: one flag block (CL_PEER_FLAG_BYTES of
+// arrival epochs, CTA ticket and step counter), the only memory besides its
+// inputs and outputs that the fused kernel touches.  It is a file-scope
+// device array, so it costs no allocation; every GPU that loads the library
+// holds these 256 bytes until the process exits.  Host code must not hand
+// `g_noalloc_flags` to a kernel: on the host the name stands for a host-side
+// copy, so its device address is looked up once per device.
+constexpr size_t kNoAllocScratchBytes = 256;
+static_assert(kNoAllocScratchBytes >= CL_PEER_FLAG_BYTES, "room for one flag block");
+static __device__ __align__(256) unsigned char g_noalloc_flags[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of the flag block on the current device (looked up on the
+// first call per device, with that device current).
+int noalloc_flag_block(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "int4gemv_fused_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(CL_ERR_INVALID_ARGUMENT,
+                    "int4gemv_fused_noalloc: device ordinal must be below 64");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_flags);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "int4gemv_fused_noalloc: cudaGetSymbolAddress(flag block)");
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return CL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -434,6 +473,37 @@ int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void*
     const clb::ShardedVariantDesc* t = clb::int4_sharded_variants(&n);
     return run_sharded(t, n, "int4gemv", variant, W_shard, scale_shard, x, M, y_peers, flag_peers,
                        rank, world, row0, N_shard, N_total, K, stream, flags, true);
+}
+
+int cl_int4gemv_fused_noalloc(const char* variant, const uint8_t* W_packed, const void* scale,
+                              const void* x, int64_t M, void* y, int64_t N, int64_t K,
+                              void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::ShardedVariantDesc* t = clb::int4_sharded_variants(&n);
+    // Every check of the launch first, so that a rejected call leaves the
+    // stream untouched.
+    if (!find_sharded(t, n, variant))
+        return fail(CL_ERR_UNKNOWN_VARIANT, std::string("int4gemv_fused_noalloc: unknown variant '") +
+                                                (variant ? variant : "(null)") + "'");
+    int rc = check_args("int4gemv_fused_noalloc", W_packed, scale, x, y, N, K, true);
+    if (rc != CL_OK) return rc;
+    if (M < 1 || M > 16)
+        return fail(CL_ERR_INVALID_ARGUMENT,
+                    "int4gemv_fused_noalloc: M must be in [1, 16] (larger batches: call again "
+                    "per 16 rows)");
+    if ((reinterpret_cast<uintptr_t>(W_packed) | reinterpret_cast<uintptr_t>(x)) & 15u)
+        return fail(CL_ERR_INVALID_ARGUMENT,
+                    "int4gemv_fused_noalloc: W_packed and x must be 16-byte aligned");
+    void* flag = nullptr;
+    rc = noalloc_flag_block(&flag);
+    if (rc != CL_OK) return rc;
+    // The block keeps the previous call's contents: start every call from zero.
+    cudaError_t e = cudaMemsetAsync(flag, 0, CL_PEER_FLAG_BYTES, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "int4gemv_fused_noalloc: clearing the flag block");
+    void* ys[2] = {y, y};  // one rank: both step parities write the caller's y
+    void* fs[1] = {flag};
+    return run_sharded(t, n, "int4gemv", variant, W_packed, scale, x, M, ys, fs, 0, 1, 0, N, N, K,
+                       stream, flags, true);
 }
 
 int cl_qgemv_sharded(const char* variant, const int8_t* W_shard, const float* scale_shard,

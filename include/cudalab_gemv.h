@@ -220,6 +220,25 @@ int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void*
                         const void* x, int64_t M, void* const* y_peers, void* const* flag_peers,
                         int rank, int world, int64_t row0, int64_t N_shard, int64_t N_total,
                         int64_t K, void* stream, uint32_t flags);
+/* No counterpart in the reference.  The fused step of cl_int4gemv_sharded on
+ * one GPU, for callers that may not allocate device memory: code whose host
+ * framework owns every device allocation and hands it only the tensors it
+ * computes on, or code that issues its GEMVs while a stream capture is open,
+ * where cudaMalloc is not allowed.  Such callers cannot make the flag block
+ * that cl_peer_alloc provides; here it lives in a fixed 256-byte array inside
+ * the library (one per GPU that loads it, held until the process exits), so
+ * the call allocates nothing.  The caller passes W_packed [N, K/2], scale
+ * [N, K/128], x [M, K] and y [M, N] (fp16, 1 <= M <= 16; larger M is rejected
+ * with CL_ERR_INVALID_ARGUMENT); y receives W x, the same bits as
+ * cl_int4gemv_ex / cl_int4gemv_batched with the same variant family.  The
+ * scratch is one flag block whatever N, K and M are.  The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture); every call clears the block on `stream` before its kernel.  All
+ * calls share the one block: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller. */
+int cl_int4gemv_fused_noalloc(const char* variant, const uint8_t* W_packed, const void* scale,
+                              const void* x, int64_t M, void* y, int64_t N, int64_t K,
+                              void* stream, uint32_t flags);
 /* Same for INT8 (W_shard int8 [N_shard, K], scale_shard fp32 [N_shard], K % 64 == 0). */
 int cl_qgemv_sharded(const char* variant, const int8_t* W_shard, const float* scale_shard,
                      const void* x, int64_t M, void* const* y_peers, void* const* flag_peers,
