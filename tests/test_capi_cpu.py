@@ -78,6 +78,25 @@ def test_status_codes_without_device(lib):
                                       None, 0, buf) == nat.CL_ERR_INVALID_ARGUMENT
 
 
+def test_noalloc_entry_rejects_before_device_work(lib):
+    # the allocation-free fused step validates everything before it looks up
+    # its device array or touches the stream, so these run without a GPU
+    fake = 1 << 20  # a 16-byte aligned, never dereferenced address
+    f = lib.cl_int4gemv_fused_noalloc
+    assert f(b"no_such", fake, fake, fake, 1, fake, 64, 256, None, 0) == \
+        nat.CL_ERR_UNKNOWN_VARIANT
+    assert f(b"int4gemv_mma", fake, fake, fake, 17, fake, 64, 256, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert "[1, 16]" in nat.last_error(lib)
+    assert f(b"int4gemv_mma", fake, fake, fake, 1, None, 64, 256, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert f(b"int4gemv_mma", fake, fake, fake, 1, fake, 64, 200, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert f(b"int4gemv_mma", fake + 2, fake, fake, 1, fake, 64, 256, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert "16-byte" in nat.last_error(lib)
+
+
 def test_product_has_no_oracle_dependency():
     """The package never imports the checker (oracle/)."""
     pkg = ROOT / "cudalab_b200"
