@@ -81,8 +81,8 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
+    def __init__(self, gpu_id: str):
+        self.idx = gpu_id
         self.samples = []
         self.proc = None
         self.t0 = self.t1 = None
@@ -302,8 +302,9 @@ def main():
         for _ in range(args.warmup):
             g.replay()
     barrier()
-    sampler = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    # nvidia-smi -i takes an index or a UUID, as CUDA_VISIBLE_DEVICES may hold either
+    vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    sampler = ClockSampler(vis[local] if local < len(vis) else str(local))
     sampler.start()
     time.sleep(0.3)
     e0 = torch.cuda.Event(enable_timing=True)
