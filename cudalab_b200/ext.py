@@ -26,6 +26,26 @@ NATIVE_NOTE = ("native kernel-loop timing: back-to-back launches issued from C++
                "Python boundary (distinct from the API-path and ncu durations)")
 
 
+def timing_result(variant: str, warmup: int, n_windows: int, launches_per_window: int,
+                  per_window_us) -> dict:
+    """The dict native_timing returns (kernels/*/bindings.cpp native_timing of
+    the reference): per-window single-launch times and their statistics."""
+    per = [float(v) for v in per_window_us]
+    s = sorted(per)
+    return {
+        "variant": variant,
+        "warmup": warmup,
+        "n_windows": n_windows,
+        "launches_per_window": launches_per_window,
+        "window_median_us": per,
+        "median_us": statistics.median(s),
+        "min_us": s[0],
+        "max_us": s[-1],
+        "mean_us": sum(s) / len(s),
+        "note": NATIVE_NOTE,
+    }
+
+
 def _chk(cond: bool, msg: str) -> None:
     if not cond:
         raise RuntimeError(msg)
@@ -180,20 +200,7 @@ class _ExtBase:
                               _stream_ptr(dev), flags, buf)
         if rc != nat.CL_OK:
             raise RuntimeError(f"native_timing failed ({rc}): {nat.last_error(self._lib)}")
-        per = [float(v) for v in buf]
-        s = sorted(per)
-        return {
-            "variant": variant,
-            "warmup": warmup,
-            "n_windows": n_windows,
-            "launches_per_window": launches_per_window,
-            "window_median_us": per,
-            "median_us": statistics.median(s),
-            "min_us": s[0],
-            "max_us": s[-1],
-            "mean_us": sum(s) / len(s),
-            "note": NATIVE_NOTE,
-        }
+        return timing_result(variant, warmup, n_windows, launches_per_window, buf)
 
 
 class Int4gemvExt(_ExtBase):
@@ -396,20 +403,7 @@ class GemvExt:
                 _stream_ptr(dev), flags, buf)
         if rc != nat.CL_OK:
             raise RuntimeError(f"native_timing failed ({rc}): {nat.last_error(self._lib)}")
-        per = [float(v) for v in buf]
-        s = sorted(per)
-        return {
-            "variant": variant,
-            "warmup": warmup,
-            "n_windows": n_windows,
-            "launches_per_window": launches_per_window,
-            "window_median_us": per,
-            "median_us": statistics.median(s),
-            "min_us": s[0],
-            "max_us": s[-1],
-            "mean_us": sum(s) / len(s),
-            "note": NATIVE_NOTE,
-        }
+        return timing_result(variant, warmup, n_windows, launches_per_window, buf)
 
 
 _EXT_TYPES = {"int4gemv": Int4gemvExt, "qgemv": QgemvExt, "gemv": GemvExt}

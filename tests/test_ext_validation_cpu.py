@@ -64,3 +64,12 @@ def test_variant_lists(e4, e8):
     assert set(e4.variants()) <= set(e4.all_variants())
     for e in (e4, e8):
         assert sorted(e.variants() + e.quarantined_variants()) == e.all_variants()
+
+
+def test_native_timing_result_shape():
+    from cudalab_b200.ext import timing_result
+    d = timing_result("int4gemv_mma", 5, 3, 8, [3.0, 1.0, 2.0])
+    assert d["window_median_us"] == [3.0, 1.0, 2.0]
+    assert (d["min_us"], d["median_us"], d["max_us"], d["mean_us"]) == (1.0, 2.0, 3.0, 2.0)
+    assert set(d) == {"variant", "warmup", "n_windows", "launches_per_window", "window_median_us",
+                      "median_us", "min_us", "max_us", "mean_us", "note"}
