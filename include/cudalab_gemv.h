@@ -222,9 +222,10 @@ int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void*
                         int64_t K, void* stream, uint32_t flags);
 /* No counterpart in the reference.  The fused step of cl_int4gemv_sharded on
  * one GPU, for callers that may not allocate device memory: code whose host
- * framework owns every device allocation and hands it only the tensors it
- * computes on, or code that issues its GEMVs while a stream capture is open,
- * where cudaMalloc is not allowed.  Such callers cannot make the flag block
+ * framework (a serving runtime, a plugin host) owns every device allocation
+ * and hands it only the tensors it computes on, or code that runs under a
+ * fixed device-memory budget that forbids further allocations.  Such callers
+ * cannot make the flag block
  * that cl_peer_alloc provides; here it lives in a fixed 256-byte array inside
  * the library (one per GPU that loads it, held until the process exits), so
  * the call allocates nothing.  The caller passes W_packed [N, K/2], scale

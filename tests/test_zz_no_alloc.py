@@ -1,6 +1,6 @@
 """cl_int4gemv_fused_noalloc, the entry point for callers that may not
-allocate device memory (their framework owns all device allocations, or they
-issue GEMVs while a stream capture is open).  It runs the fused single-GPU
+allocate device memory (their framework owns all device allocations, or a
+fixed memory budget forbids more).  It runs the fused single-GPU
 step with its flag block in a fixed array inside the library; its output must
 match the regular entry point, cl_int4gemv_ex, on consecutive calls (the
 array keeps the previous call's contents, so a second call checks that each
