@@ -45,6 +45,7 @@ PROTOTYPES = {
     "cl_version": (_cs, []),
     "cl_last_error": (_cs, []),
     "cl_device_status": (_int, [_int, ctypes.POINTER(_int)]),
+    "cl_set_wait_budget": (_int, [_i64, ctypes.POINTER(_i64)]),
     "cl_int4gemv": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "cl_int4gemv_ex": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _u32]),
     "cl_int4gemv_native_timing": (_int, [_cs, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
@@ -118,6 +119,15 @@ def list_variants(kind: str, which: int) -> list[str]:
         raise RuntimeError(f"list_variants failed ({rc}): {last_error(lib)}")
     text = buf.value.decode()
     return [v for v in text.split("\n") if v]
+
+
+def set_wait_budget(cycles: int) -> int:
+    """Bound (SM cycles) of the device-side waits of later launches; <= 0
+    restores the default.  Returns the previous bound."""
+    lib = load()
+    prev = _i64(0)
+    lib.cl_set_wait_budget(int(cycles), ctypes.byref(prev))
+    return prev.value
 
 
 def device_status(clear: bool = False) -> int:

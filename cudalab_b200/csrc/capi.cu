@@ -5,6 +5,7 @@
 // status codes + a per-thread error message, and the native launch-loop timer.
 // Tensor-level checks (dims, dtypes, devices, contiguity) are made by the host
 // wrapper before the call, in the order of the reference extension.
+#include <cuda.h>  // CUcontext / CUresult types; the driver functions come via the runtime
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -242,10 +243,46 @@ static __device__ __align__(256) unsigned char g_noalloc_flags[kNoAllocScratchBy
 
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+struct NoAllocSlot {
+    void* addr = nullptr;
+    unsigned long long ctx_id = 0;  // context the address belongs to (0: unknown)
+};
+NoAllocSlot g_noalloc_slot[kNoAllocMaxDevices];
 
-// Device address of the flag block on the current device (looked up on the
-// first call per device, with that device current).
+// Unique id of the calling thread's current CUDA context, 0 when the driver
+// cannot tell.  The two driver functions are fetched through the runtime, so
+// the library keeps no link-time dependency on the driver library.
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+        get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// Device address of the flag block on the current device.  Set-up happens on
+// the first call per device, with that device current, and again whenever
+// the device's current context differs from the one the address was looked
+// up in (after a cudaDeviceReset the runtime loads the library's module into
+// a new context, at a new address); when the context id cannot be read the
+// address is looked up on every call.
 int noalloc_flag_block(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -254,14 +291,17 @@ int noalloc_flag_block(void** out) {
         return fail(CL_ERR_INVALID_ARGUMENT,
                     "int4gemv_fused_noalloc: device ordinal must be below 64");
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_addr[dev] == nullptr) {
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    const unsigned long long ctx = slot.addr ? current_context_id() : 0;
+    if (slot.addr == nullptr || ctx == 0 || ctx != slot.ctx_id) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_flags);
         if (e != cudaSuccess)
             return cuda_fail(e, "int4gemv_fused_noalloc: cudaGetSymbolAddress(flag block)");
-        g_noalloc_addr[dev] = p;
+        slot.addr = p;
+        slot.ctx_id = current_context_id();  // the lookup made the context current
     }
-    *out = g_noalloc_addr[dev];
+    *out = slot.addr;
     return CL_OK;
 }
 
@@ -277,6 +317,12 @@ int cl_device_status(int clear, int* status_out) {
     if (!status_out) return fail(CL_ERR_INVALID_ARGUMENT, "status_out is null");
     cudaError_t e = clb::read_device_status(clear, status_out);
     if (e != cudaSuccess) return cuda_fail(e, "read device status");
+    return CL_OK;
+}
+
+int cl_set_wait_budget(int64_t cycles, int64_t* previous) {
+    const long long prev = clb::set_wait_budget((long long)cycles);
+    if (previous) *previous = (int64_t)prev;
     return CL_OK;
 }
 

@@ -10,7 +10,7 @@
 //     fp16 x fp16 products, one rounding per term) or packed `fma.rn.f32x2`.
 //
 // Every spin-wait is bounded by the SM cycle counter; on expiry the kernel records
-// an error code in a per-translation-unit device word that the host reads
+// an error code in the library's device status word that the host reads
 // through the C ABI (cl_device_status) and returns without touching more
 // memory.
 #pragma once
@@ -32,9 +32,12 @@ constexpr int kMaxSliceBytes = kConsumerThreads * kChunkBytes;               // 
 constexpr int kRingBytes = 64 * 1024;               // weight staging ring per CTA
 constexpr int kMaxStages = 16;
 constexpr int kScaleSmemBytes = 32 * 1024;          // per-CTA cache of group scales
-// Bound of every spin-wait, in SM clock cycles (~2 s at 2 GHz).  The SM-local
-// cycle counter is used because reading %globaltimer is a slow,
-// long-latency operation that would dominate a short wait.
+// Default bound of every spin-wait, in SM clock cycles (~2 s at 2 GHz).  The
+// SM-local cycle counter is used because reading %globaltimer is a slow,
+// long-latency operation that would dominate a short wait.  The bound a kernel
+// uses is a launch parameter (GemvGeom / MmaGeom `wait_cycles`), set from the
+// process-wide value of cl_set_wait_budget, so a test can make a wait expire
+// after a millisecond.
 constexpr long long kWaitTimeoutCycles = 4000000000ll;
 
 // Error codes written to the device status word.
@@ -45,12 +48,17 @@ constexpr int kStatusTimeoutScale = 3;   // consumer gave up waiting for scales
 constexpr int kStatusTimeoutDrain = 4;   // producer gave up draining its copies
 constexpr int kStatusTimeoutPeer = 5;    // a sharded GEMV gave up waiting for a peer rank
 
-// Per-device status word for bounded waits (one per translation unit that
-// includes this header; read through the C ABI).  The first code recorded
-// since the last clear wins.
-static __device__ int g_status;
+// Per-device status word for bounded waits, read and cleared through the C ABI
+// (cl_device_status).  The first code recorded since the last clear wins.
+// Exactly one translation unit defines it: the one that holds every kernel
+// with a bounded wait (gemv_kernels.cu defines CLB_STATUS_OWNER before
+// including this header).  Other translation units see neither the word nor
+// record_status, so a kernel there cannot write a status nobody reads.
+#ifdef CLB_STATUS_OWNER
+__device__ int g_status;
 
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_status, 0, code); }
+#endif
 
 // ---------------------------------------------------------------------------
 // Small PTX wrappers.
@@ -94,13 +102,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait on one mbarrier phase. Returns false when the budget expired.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Bounded wait on one mbarrier phase: at most `budget` SM cycles.  Returns
+// false when the budget expired.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  long long budget) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
 #pragma unroll 1
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitTimeoutCycles) return false;
+        if (clock64() - t0 > budget) return false;
     }
     return true;
 }

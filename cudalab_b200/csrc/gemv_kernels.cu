@@ -17,11 +17,15 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
 #include <utility>
 
+// This translation unit holds every kernel with a bounded wait, so it owns the
+// device status word (gemv_common.cuh).
+#define CLB_STATUS_OWNER 1
 #include "gemv_launch.h"
 #include "gemv_vector.cuh"
 #include "gemv_mma.cuh"
@@ -91,6 +95,9 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 
+// Bound of the device-side waits of every launch (SM cycles), process-wide.
+std::atomic<long long> g_wait_budget{kWaitTimeoutCycles};
+
 int sm_count(int dev) {
     static int cache[kMaxDevices] = {0};
     if (dev < 0 || dev >= kMaxDevices) return 148;
@@ -142,6 +149,7 @@ GemvGeom make_geom(int64_t N, int64_t K, bool int4, bool bulk, int num_sms) {
     g.thread_rows = kConsumerThreads / g.chunks;
     g.tile_rows = kRowsPerThread * g.thread_rows;
     g.groups = int4 ? (int32_t)(K / 128) : 1;
+    g.wait_cycles = g_wait_budget.load(std::memory_order_relaxed);
     const int64_t scale_row_bytes = int4 ? (int64_t)g.groups * 2 : 4;
     int64_t ctas = std::min<int64_t>(N, (int64_t)num_sms * (bulk ? 1 : 2));
     const int64_t max_rows_by_scale = std::max<int64_t>(1, kScaleSmemBytes / scale_row_bytes);
@@ -264,6 +272,7 @@ cudaError_t per_row(const GemvArgs& a, cudaStream_t s, unsigned flags) {
 bool make_mma_geom(int64_t N, int64_t K, int64_t M, int kind, int num_sms, int ctas_per_sm,
                    int64_t max_groups, MmaGeom& g) {
     g = MmaGeom{};
+    g.wait_cycles = g_wait_budget.load(std::memory_order_relaxed);
     g.N = N;
     g.K = K;
     g.M = (int32_t)M;
@@ -503,6 +512,21 @@ const VariantDesc kInt4Variants[] = {
     {"int4gemv_mma_w8", launch_mma<MmaInt4, 8, 1>, false},
     {"int4gemv_mma_w8c2", launch_mma<MmaInt4, 8, 2>, false},
     {"int4gemv_mma_w16", launch_mma<MmaInt4, 16, 1>, false},
+    // The reference's variant names (kernels/int4gemv/*.cu registrars), each
+    // bound to the kernel here that fills the same role, so a caller that
+    // dispatches by those strings runs unmodified:
+    //   vec16_row   16-byte vector loads, no row tiling   -> register-direct
+    //               streaming kernel (int4gemv_vec16_row.cu:143)
+    //   rowtile4/8  x reused across a tile of rows         -> tensor-core
+    //               kernel, 4 / 8 warps per CTA sharing the staged x
+    //               (int4gemv_rowtile4.cu:175, int4gemv_rowtile8.cu:172)
+    //   rowtile4_hx the incumbent                          -> production
+    //               tensor-core kernel, geometry per call
+    //               (int4gemv_rowtile4_hx.cu:173)
+    {"int4gemv_vec16_row", per_row<launch_vec1<Int4Fmt, MathF16, false>>, false},
+    {"int4gemv_rowtile4", launch_mma<MmaInt4, 4, 1>, false},
+    {"int4gemv_rowtile8", launch_mma<MmaInt4, 8, 1>, false},
+    {"int4gemv_rowtile4_hx", launch_mma_auto<MmaInt4>, false},
 };
 
 const VariantDesc kInt8Variants[] = {
@@ -517,6 +541,20 @@ const VariantDesc kInt8Variants[] = {
     {"qgemv_mma_w8", launch_mma<MmaInt8, 8, 1>, false},
     {"qgemv_mma_w8c2", launch_mma<MmaInt8, 8, 2>, false},
     {"qgemv_mma_w16", launch_mma<MmaInt8, 16, 1>, false},
+    // The reference's variant names (kernels/qgemv/*.cu registrars) bound to
+    // the kernels here that fill the same role:
+    //   vec16_row        the dispatch incumbent -> production tensor-core
+    //                    kernel (qgemv_vec16_row.cu:99)
+    //   vec16_scale      row scale applied once at the row end -> tensor-core
+    //                    kernel with 8-warp CTAs (qgemv_vec16_scale.cu:105)
+    //   warp_vec16       one warp per row, 16-byte loads into registers ->
+    //                    register-direct streaming kernel (qgemv_warp_vec16.cu:110)
+    //   warp_vec16_ilp4  more loads in flight per warp -> shared-memory ring
+    //                    fed by bulk copies (qgemv_warp_vec16_ilp4.cu:124)
+    {"qgemv_vec16_row", launch_mma_auto<MmaInt8>, false},
+    {"qgemv_vec16_scale", launch_mma<MmaInt8, 8, 1>, false},
+    {"qgemv_warp_vec16", per_row<launch_vec1<Int8Fmt, MathF16, false>>, false},
+    {"qgemv_warp_vec16_ilp4", per_row<launch_vec1<Int8Fmt, MathF16, true>>, false},
 };
 
 }  // namespace
@@ -560,18 +598,20 @@ const ShardedVariantDesc* int8_sharded_variants(int* count) {
 }
 
 cudaError_t read_device_status(int clear, int* status) {
-    int v = 0, m = 0;
+    int v = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int));
-
     if (e != cudaSuccess) return e;
     if (clear) {
         const int zero = 0;
         e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
-
         if (e != cudaSuccess) return e;
     }
-    *status = v ? v : m;
+    *status = v;
     return cudaSuccess;
+}
+
+long long set_wait_budget(long long cycles) {
+    return g_wait_budget.exchange(cycles > 0 ? cycles : kWaitTimeoutCycles);
 }
 
 }  // namespace clb

@@ -67,4 +67,8 @@ cudaError_t launch_f16_scalar(const void* W, const void* scale, const void* x, v
 // current device.
 cudaError_t read_device_status(int clear, int* status);
 
+// Sets the bound of the device-side waits of later launches (SM cycles; <= 0
+// restores the default of about two seconds) and returns the previous bound.
+long long set_wait_budget(long long cycles);
+
 }  // namespace clb

@@ -79,6 +79,7 @@ struct MmaGeom {
     int32_t max_rows;             // rows of the largest row group
     int32_t early_x;              // x is not written by the preceding kernel
     int32_t free_y;               // y is not accessed by any kernel still in flight
+    long long wait_cycles;        // bound of the peer-flag wait (SM cycles)
 };
 
 constexpr int kZeroRegion = 256;  // bytes of zeros ahead of the staged activations
@@ -221,7 +222,8 @@ struct PeerOut {
 // one per peer as st.release would imply) publish every CTA's stores (through
 // the ticket atomics).  Loops run over the compile-time peer slots so that
 // `po` stays in the parameter space (no local copy).
-__device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned epoch) {
+__device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned epoch,
+                                                     long long budget) {
     unsigned* mine = po.flag[po.rank];
     __threadfence_system();
     const unsigned prev = atomicAdd(mine + kTicket, 1u);
@@ -235,7 +237,7 @@ __device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned
     bool ok = true;
     for (int q = 0; q < po.world && ok; ++q) {
         while ((int)(ld_acquire_sys(mine + q) - epoch) < 0) {
-            if (clock64() - t0 > kWaitTimeoutCycles) {
+            if (clock64() - t0 > budget) {
                 record_status(kStatusTimeoutPeer);
                 ok = false;
                 break;
@@ -845,7 +847,7 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     }
     if constexpr (kPeer) {
         __syncthreads();
-        if (tid == 0) peer_arrive_and_wait(po, epoch);
+        if (tid == 0) peer_arrive_and_wait(po, epoch, g.wait_cycles);
     } else {
         if (g.free_y && blockIdx.x == 0) pdl_wait_prior_grids();
     }

@@ -52,6 +52,7 @@ struct GemvGeom {
     int32_t scale_smem;   // bytes of the staged scale block
     int32_t ring_bytes;   // bytes reserved for the ring (0 for register-direct)
     int32_t ctas;         // grid size
+    long long wait_cycles;  // bound of every mbarrier wait (SM cycles)
 };
 
 // ---------------------------------------------------------------------------
@@ -369,7 +370,7 @@ gemv_vec_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
                 if (lane == 0) {
                     if (it >= g.stages) {
                         const uint32_t par = (uint32_t)((it / g.stages) - 1) & 1u;
-                        if (!mbar_wait_bounded(empty0 + 8 * st, par)) ok = 0;
+                        if (!mbar_wait_bounded(empty0 + 8 * st, par, g.wait_cycles)) ok = 0;
                     }
                     if (ok) mbar_arrive_expect_tx(full0 + 8 * st, bytes);
                 }
@@ -401,7 +402,8 @@ gemv_vec_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
                 for (int st = 0; st < used; ++st) {
                     const int last = st + ((issued - 1 - st) / g.stages) * g.stages;
                     const uint32_t par = (uint32_t)(last / g.stages) & 1u;
-                    if (!mbar_wait_bounded(full0 + 8 * st, par)) record_status(kStatusTimeoutDrain);
+                    if (!mbar_wait_bounded(full0 + 8 * st, par, g.wait_cycles))
+                        record_status(kStatusTimeoutDrain);
                 }
             }
             return;
@@ -457,7 +459,7 @@ gemv_vec_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
             const int st = kBulk ? it % g.stages : 0;
             if constexpr (kBulk) {
                 const uint32_t par = (uint32_t)(it / g.stages) & 1u;
-                if (!failed && !mbar_wait_bounded(full0 + 8 * st, par)) {
+                if (!failed && !mbar_wait_bounded(full0 + 8 * st, par, g.wait_cycles)) {
                     record_status(kStatusTimeoutFull);
                     failed = true;
                 }

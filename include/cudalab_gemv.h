@@ -78,6 +78,15 @@ const char* cl_last_error(void);
  * device: 0 = no device-side wait expired since the last clear. */
 int cl_device_status(int clear, int* status_out);
 
+/* No counterpart in the reference (its kernels never wait on device-side
+ * events).  Sets the bound of every device-side wait of later launches, in SM
+ * clock cycles (default 4e9, about two seconds at 2 GHz; cycles <= 0 restores
+ * it), process-wide, and writes the previous bound to *previous (may be
+ * NULL).  A wait that runs out records CL_ERR_DEVICE_TIMEOUT-class status
+ * codes in cl_device_status and its kernel returns; a short bound lets a test
+ * make a wait expire without holding the GPU. */
+int cl_set_wait_budget(int64_t cycles, int64_t* previous);
+
 /* ---- INT4 W4A16 ---- */
 
 /* Replaces the pybind entry points `forward` / `forward_into` of
@@ -234,9 +243,12 @@ int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void*
  * cl_int4gemv_ex / cl_int4gemv_batched with the same variant family.  The
  * scratch is one flag block whatever N, K and M are.  The first call on a
  * device looks up the array's device address (make it before any stream
- * capture); every call clears the block on `stream` before its kernel.  All
- * calls share the one block: calls that overlap on the GPU (other streams,
- * other threads) race and must be serialised by the caller. */
+ * capture); so does the first call after the device's context changed (e.g.
+ * after cudaDeviceReset, which loads the library's device code again at a new
+ * address), which should likewise come before any capture.  Every call clears
+ * the block on `stream` before its kernel.  All calls share the one block:
+ * calls that overlap on the GPU (other streams, other threads) race and must
+ * be serialised by the caller. */
 int cl_int4gemv_fused_noalloc(const char* variant, const uint8_t* W_packed, const void* scale,
                               const void* x, int64_t M, void* y, int64_t N, int64_t K,
                               void* stream, uint32_t flags);

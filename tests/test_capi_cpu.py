@@ -113,3 +113,15 @@ def test_library_is_sm100a_build():
 def test_torch_cpu_only_here_or_gpu():
     # documents the environment split: this file never needs a device
     assert isinstance(torch.cuda.is_available(), bool)
+
+
+def test_wait_budget_roundtrip(lib):
+    """The device-wait bound is host state: set, read back, and restored to
+    the default by a non-positive value (no device work)."""
+    prev = nat.set_wait_budget(12345)
+    try:
+        assert nat.set_wait_budget(777) == 12345
+        assert nat.set_wait_budget(0) == 777
+        assert nat.set_wait_budget(0) == 4_000_000_000  # the default
+    finally:
+        nat.set_wait_budget(prev)

@@ -66,6 +66,22 @@ def test_variant_lists(e4, e8):
         assert sorted(e.variants() + e.quarantined_variants()) == e.all_variants()
 
 
+# Every variant name the reference registers (kernels/int4gemv/*.cu and
+# kernels/qgemv/*.cu registrars) dispatches here, so callers that name them
+# (e.g. its native-timing script) run unmodified; the -m gpu suites run the
+# 50-case, negative and golden checks over every listed variant.
+REFERENCE_INT4 = ["int4gemv_baseline", "int4gemv_vec16_row", "int4gemv_rowtile4",
+                  "int4gemv_rowtile8", "int4gemv_rowtile4_hx"]
+REFERENCE_INT8 = ["qgemv_baseline", "qgemv_vec16_row", "qgemv_vec16_scale", "qgemv_warp_vec16",
+                  "qgemv_warp_vec16_ilp4"]
+
+
+def test_reference_variant_names_dispatch(e4, e8):
+    assert set(REFERENCE_INT4) <= set(e4.variants())
+    assert set(REFERENCE_INT8) <= set(e8.variants())
+    assert not e4.quarantined_variants() and not e8.quarantined_variants()
+
+
 def test_native_timing_result_shape():
     from cudalab_b200.ext import timing_result
     d = timing_result("int4gemv_mma", 5, 3, 8, [3.0, 1.0, 2.0])

@@ -41,7 +41,7 @@ def test_correctness_suite(ext, variant):
 @pytest.mark.parametrize("variant", ALL)
 def test_negative_suite(ext, variant):
     doc = run_negative_suite(ext, variant=variant)
-    bad = [(c["id"], c["status"], c["message"]) for c in doc["cases"] if not c.get("pass")]
+    bad = [(c["id"], c["outcome"], c["first_line"]) for c in doc["cases"] if not c.get("pass")]
     assert doc["summary"]["all_pass"] and doc["summary"]["n_total"] == 24, bad
 
 

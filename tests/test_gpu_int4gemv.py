@@ -38,13 +38,13 @@ def test_layer_a_suite(ext, variant):
     s = summarize(res)
     bad = [(r.shape, r.mode, r.arith_max_ratio) for r in res if not r.passed]
     assert s["all_pass"] and s["n_total"] == 50, bad
-    nat.device_status(clear=True) == 0
+    assert nat.device_status(clear=True) == 0
 
 
 @pytest.mark.parametrize("variant", _variants())
 def test_negative_suite(ext, variant):
     doc = run_negative_suite(ext, variant=variant)
-    bad = [(c["id"], c["status"], c["message"]) for c in doc["cases"] if not c.get("pass")]
+    bad = [(c["id"], c["outcome"], c["first_line"]) for c in doc["cases"] if not c.get("pass")]
     assert doc["summary"]["all_pass"] and doc["summary"]["n_total"] == 30, bad
 
 
