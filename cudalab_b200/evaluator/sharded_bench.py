@@ -94,6 +94,140 @@ def time_steps(ops, x, flags, steps, reps, dev):
     return float(us.item()), int(stat.item())
 
 
+# ---------------------------------------------------------------------------
+# Config 4 of the north-star workload at the run's world size: the 70B-class
+# MLP shapes, INT4 G=128, M in {1, 4, 16}, fused and NCCL completion, with
+# an in-run parity check.  bench.py calls config4_block on every rank.
+# ---------------------------------------------------------------------------
+CONFIG4_SHAPES = ((28672, 8192), (8192, 28672))
+CONFIG4_BATCHES = (1, 4, 16)
+CONFIG4_FLAGS = 3  # PDL | inputs ready: x is replicated and not produced by the step before
+
+
+def _device_int4(N: int, K: int, seed: int, dev) -> tuple[torch.Tensor, torch.Tensor]:
+    """A seeded fp16 N(0, 0.02^2) matrix generated and quantised on the device
+    (the device quantiser is byte-identical to the reference's quantize_w)."""
+    from cudalab_b200.int4gemv_quantize import quantize_w_device
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    W = (torch.randn(N, K, generator=g, device=dev) * 0.02).half()
+    Wp, s = quantize_w_device(W)
+    del W
+    return Wp, s
+
+
+def _x_rows(M: int, K: int, seed: int, dev) -> torch.Tensor:
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return torch.randn(M, K, generator=g, device=dev).half()
+
+
+def _config4_parity(N, K, world, rank, dev, batches, n_sample=64) -> dict:
+    """Fused == NCCL bit for bit, this rank's rows == the single-GPU kernel on
+    its shard bit for bit, and sampled rows inside the reference's fixed
+    arithmetic bound (int4gemv_correctness.arith_ratio), for every M.  Every
+    rank builds the same full matrix; a checksum all-reduce confirms it."""
+    from cudalab_b200.build import build
+    from cudalab_b200.int4gemv_correctness import arith_ratio
+    ext = build("int4gemv")
+    Wp, s = _device_int4(N, K, 4242 + N, dev)
+    ck = torch.tensor([int(Wp.view(torch.int32).sum().item()) & 0x7fffffff], device=dev,
+                      dtype=torch.int64)
+    lo, hi = ck.clone(), ck.clone()
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    same_w = bool(lo.item() == hi.item())
+    row0, n = shard_rows(N, world, rank)
+    Ws, ss = Wp[row0:row0 + n].contiguous(), s[row0:row0 + n].contiguous()
+    rows = torch.randperm(N, generator=torch.Generator().manual_seed(N + K))[:n_sample]
+    Wp_rows, s_rows = Wp[rows.to(dev)].cpu(), s[rows.to(dev)].cpu()
+    worst, fused_eq_nccl, shard_eq_single, finite = 0.0, True, True, True
+    for M in batches:
+        X = _x_rows(M, K, 77 + M, dev)
+        xin = X[0] if M == 1 else X
+        fused = ShardedGemv("int4gemv", Ws, ss, N, K, mode="fused", max_batch=M)
+        nccl = ShardedGemv("int4gemv", Ws, ss, N, K, mode="nccl", max_batch=M)
+        try:
+            for fl in (0, CONFIG4_FLAGS):
+                y_f = fused.forward(xin, flags=fl).clone().view(M, N)
+                y_n = nccl.forward(xin, flags=fl).clone().view(M, N)
+                y_1 = (ext.forward("int4gemv_mma", Ws, ss, X[0], flags=fl)[None] if M == 1
+                       else ext.forward_batched("int4gemv_mma", Ws, ss, X, flags=fl))
+                torch.cuda.synchronize(dev)
+                fused_eq_nccl &= bool(torch.equal(y_f, y_n))
+                shard_eq_single &= bool(torch.equal(y_f[:, row0:row0 + n], y_1))
+                finite &= bool(torch.isfinite(y_f.float()).all().item())
+                yc, xc = y_f[:, rows.to(dev)].cpu(), X.cpu()
+                for m in range(M):
+                    r, _, _ = arith_ratio(yc[m], Wp_rows, s_rows, xc[m])
+                    worst = max(worst, r)
+        finally:
+            fused.close()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+    status = nat.device_status(clear=True)
+    ok = torch.tensor([int(same_w and fused_eq_nccl and shard_eq_single and finite
+                           and worst <= 1.0 and status == 0)], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    wr = torch.tensor([worst], device=dev, dtype=torch.float64)
+    dist.all_reduce(wr, op=dist.ReduceOp.MAX)
+    del Wp, s, Ws, ss
+    return {"pass": bool(ok.item()), "fused_eq_nccl": fused_eq_nccl,
+            "shard_rows_eq_single_gpu": shard_eq_single, "same_weights_all_ranks": same_w,
+            "max_arith_ratio_sampled": round(float(wr.item()), 6), "sampled_rows": n_sample}
+
+
+def config4_block(world: int, rank: int, dev, peak: float, steps: int = 32, reps: int = 10,
+                  batches=CONFIG4_BATCHES, modes=("fused", "nccl"), parity: bool = True) -> dict:
+    """Time config 4 at this world size and check its parity.  Needs an
+    initialised process group (NCCL) of `world` ranks, one GPU each.  Returns
+    (on every rank) {"cases": [...], "parity": {...}}; each case has the
+    max-over-ranks us per step and the fraction of world x the measured
+    per-GPU HBM bandwidth reached on the algorithmic bytes of the full
+    matrix."""
+    cases = []
+    for N, K in CONFIG4_SHAPES:
+        row0, n = shard_rows(N, world, rank)
+        shard_bytes = n * K // 2 + n * K // 64
+        pool = max(2, -(-2 * L2_BYTES // shard_bytes))
+        pool += pool % 2
+        shards = [_device_int4(n, K, 1000 + 97 * rank + i, dev) for i in range(pool)]
+        for M in batches:
+            x = _x_rows(M, K, 7, dev)
+            x = x[0] if M == 1 else x
+            algo = algorithmic_bytes_int4(N, K, M)
+            rec = {"shape": f"{N}x{K}", "M": M}
+            for mode in modes:
+                peers = PeerBuffers(N, max_batch=M) if mode == "fused" else None
+                ops = [ShardedGemv("int4gemv", w, s, N, K, mode=mode, peers=peers, max_batch=M)
+                       for w, s in shards]
+                t, status = time_steps(ops, x, CONFIG4_FLAGS, steps, reps, dev)
+                gbs = algo / (t * 1e-6) / 1e9
+                rec[mode] = {"us_per_step": round(t, 3),
+                             "frac_of_aggregate_hbm": round(gbs / (world * peak), 4),
+                             "device_status": status}
+                for op in ops:
+                    op.close()
+                if peers is not None:
+                    torch.cuda.synchronize(dev)
+                    dist.barrier()
+                    peers.close()
+            cases.append(rec)
+        del shards
+        torch.cuda.empty_cache()
+    out = {"workload": "int4gemv row-sharded, x replicated, y all-gathered on every rank; "
+                       f"pool of weight shards > 2x L2 per rank; flags {CONFIG4_FLAGS}",
+           "n_gpus": world, "cases": cases}
+    if parity:
+        par = {}
+        for N, K in CONFIG4_SHAPES:
+            par[f"{N}x{K}"] = _config4_parity(N, K, world, rank, dev, batches)
+            torch.cuda.empty_cache()
+        out["parity"] = par
+        out["sharded_parity"] = all(v["pass"] for v in par.values())
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--kinds", default="int4gemv")

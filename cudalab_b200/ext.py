@@ -51,8 +51,32 @@ def _chk(cond: bool, msg: str) -> None:
         raise RuntimeError(msg)
 
 
+_U8, _I8, _F16, _F32 = torch.uint8, torch.int8, torch.float16, torch.float32
+# Raw handle of the current stream / index of the current device without
+# building Python objects (about 0.1 us each instead of several us).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_cur_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def _stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _stream_of(idx: int) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+def _device_is_current(idx: int) -> bool:
+    return (_cur_device() if _cur_device is not None else torch.cuda.current_device()) == idx
+
+
+def _same_device(idx: int, *ts) -> bool:
+    for t in ts:
+        if not t.is_cuda or t.get_device() != idx:
+            return False
+    return True
 
 
 class _ExtBase:
@@ -62,6 +86,8 @@ class _ExtBase:
     def __init__(self) -> None:
         self._lib = nat.load()
         self._cache = {}
+        # every registered name (normal and quarantined) -> its bytes for the C call
+        self._encoded = {v: v.encode() for v in self.all_variants()}
 
     # ---- variant registry ----
     def variants(self) -> list[str]:
@@ -117,26 +143,41 @@ class _ExtBase:
         return K
 
     def _launch(self, name: str, W, scale, x, out, flags: int = 0) -> None:
-        N, K = W.size(0), self._k_of(W)
-        dev = W.device
-        with torch.cuda.device(dev):
-            rc = self._call(name.encode(), W.data_ptr(), scale.data_ptr(), x.data_ptr(),
-                            out.data_ptr(), N, K, _stream_ptr(dev), flags)
+        idx = W.get_device()
+        args = (self._encoded.get(name) or name.encode(), W.data_ptr(), scale.data_ptr(),
+                x.data_ptr(), out.data_ptr(), W.size(0), self._k_of(W))
+        if _device_is_current(idx):
+            rc = self._call(*args, _stream_of(idx), flags)
+        else:
+            with torch.cuda.device(idx):
+                rc = self._call(*args, _stream_of(idx), flags)
         if rc != nat.CL_OK:
             raise RuntimeError(f"{self.kind} launch failed ({rc}): {nat.last_error(self._lib)}")
 
+    # Success-path predicate: true only when every ordered check of
+    # _check_variant / _validate_inputs / _validate_out would pass (it may be
+    # stricter, never looser), so the common call skips building messages; on
+    # False the ordered checks run and raise the reference's message.
+    def _fast_ok(self, variant, W, scale, x, out) -> bool:
+        if variant not in self._encoded or not self._fast_inputs(W, scale, x):
+            return False
+        return (out is None or (out.dtype is _F16 and out.shape == (W.shape[0],)
+                                and out.is_contiguous() and _same_device(W.get_device(), out)))
+
     # ---- public API (names and keyword names of the reference module) ----
     def forward(self, variant: str, W, scale, x, flags: int = 0) -> torch.Tensor:
-        self._check_variant(variant)
-        self._validate_inputs(W, scale, x)
+        if not self._fast_ok(variant, W, scale, x, None):
+            self._check_variant(variant)
+            self._validate_inputs(W, scale, x)
         out = torch.empty(W.size(0), dtype=torch.float16, device=W.device)
         self._launch(variant, W, scale, x, out, flags)
         return out
 
     def forward_into(self, variant: str, W, scale, x, out, flags: int = 0) -> None:
-        self._check_variant(variant)
-        self._validate_inputs(W, scale, x)
-        self._validate_out(W, out)
+        if not self._fast_ok(variant, W, scale, x, out):
+            self._check_variant(variant)
+            self._validate_inputs(W, scale, x)
+            self._validate_out(W, out)
         self._launch(variant, W, scale, x, out, flags)
 
     # ---- batched activations (no reference counterpart; English messages) ----
@@ -217,6 +258,17 @@ class Int4gemvExt(_ExtBase):
     def _k_of(self, W) -> int:
         return 2 * W.size(1)
 
+    @staticmethod
+    def _fast_inputs(Wp, scale, x) -> bool:
+        if Wp.dtype is not _U8 or Wp.dim() != 2 or not Wp.is_contiguous():
+            return False
+        n, kh = Wp.shape
+        if n <= 0 or kh <= 0 or kh % 64:  # K = 2 kh, K % 128 == 0
+            return False
+        return (scale.dtype is _F16 and scale.shape == (n, kh // 64) and scale.is_contiguous()
+                and x.dtype is _F16 and x.shape == (2 * kh,) and x.is_contiguous()
+                and Wp.is_cuda and _same_device(Wp.get_device(), scale, x))
+
     def _validate_w(self, Wp: torch.Tensor) -> None:
         _chk(Wp.dim() == 2, f"W_packed 必须是 2 维 (N, K/2)，实际 {Wp.dim()} 维 "
                             "(W_packed must be 2-D)")
@@ -262,6 +314,17 @@ class QgemvExt(_ExtBase):
 
     def _k_of(self, W) -> int:
         return W.size(1)
+
+    @staticmethod
+    def _fast_inputs(Wq, scale, x) -> bool:
+        if Wq.dtype is not _I8 or Wq.dim() != 2 or not Wq.is_contiguous():
+            return False
+        n, k = Wq.shape
+        if n <= 0 or k <= 0:
+            return False
+        return (scale.dtype is _F32 and scale.shape == (n,) and scale.is_contiguous()
+                and x.dtype is _F16 and x.shape == (k,) and x.is_contiguous()
+                and Wq.is_cuda and _same_device(Wq.get_device(), scale, x))
 
     def _validate_w(self, Wq: torch.Tensor) -> None:
         _chk(Wq.dim() == 2, f"W_q 必须是 2 维 (N, K)，实际 {Wq.dim()} 维 (W_q must be 2-D)")

@@ -3,7 +3,7 @@
   * the 50-case layer-A suite (10 shapes x 5 modes) per variant;
   * the 30-case negative suite per variant;
   * the reference's golden vectors (tests/golden) on every variant;
-  * full-size BASELINE shapes against the numpy oracle's fixed bound;
+  * full-size north-star shapes (4096x4096, the 7B sweep, the 70B MLP shapes) against the numpy oracle's fixed bound;
   * determinism, PDL launches, CUDA-graph capture, native timing.
 """
 from pathlib import Path
