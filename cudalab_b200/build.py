@@ -32,7 +32,10 @@ STAMP = LIB_DIR / "libcudalab_gemv.stamp.json"
 HEADER = ROOT / "include" / "cudalab_gemv.h"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared"]
+# --split-compile 0: the optimiser and ptxas work on a translation unit's
+# kernels in parallel on every host core (the kernel unit holds dozens of
+# template instantiations)
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--split-compile", "0"]
 SOURCES = ["gemv_kernels.cu", "gemv_dense.cu", "quantize.cu", "capi.cu"]
 
 
@@ -68,16 +71,32 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     if not force and library_is_current():
         return LIB_PATH
     LIB_DIR.mkdir(parents=True, exist_ok=True)
+    obj_dir = LIB_DIR / "obj"
+    obj_dir.mkdir(exist_ok=True)
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *[str(CSRC / s) for s in SOURCES], "-o", str(tmp)]
+    nvcc = _nvcc()
+    # every translation unit compiles concurrently, then one link
+    jobs = []
+    for src in SOURCES:
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-c", str(CSRC / src),
+               "-o", str(obj_dir / (Path(src).stem + ".o"))]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd))
+        jobs.append(subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                                     text=True))
+    logs = [(src, p.communicate()[0], p.returncode) for src, p in zip(SOURCES, jobs)]
+    failed = [(src, out) for src, out, rc in logs if rc != 0]
+    if failed:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(f"{s}:\n{o}" for s, o in failed))
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
-    proc = subprocess.run(cmd, capture_output=True, text=True)
+        for _, out, _ in logs:
+            print(out)
+    link = [nvcc, *ARCH_FLAGS, "-shared",
+            *[str(obj_dir / (Path(s).stem + ".o")) for s in SOURCES], "-o", str(tmp)]
+    proc = subprocess.run(link, capture_output=True, text=True)
     if proc.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + proc.stdout + proc.stderr)
-    if verbose:
-        print(proc.stdout + proc.stderr)
+        raise RuntimeError("nvcc link failed:\n" + proc.stdout + proc.stderr)
     os.replace(tmp, LIB_PATH)
     STAMP.write_text(json.dumps({"hash": _fingerprint(), "sources": SOURCES,
                                  "flags": ARCH_FLAGS + NVCC_FLAGS}, indent=2))
