@@ -434,7 +434,50 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
                                          int lb0, const MmaGeom& g, int gq, int t,
                                          MmaAcc<kNB>& sacc) {
     constexpr int kBlk = Fmt::kBlockWords;
-    if constexpr (kNB == 0) {
+    if constexpr (kNB == 0 && Fmt::kGroupScale) {
+        // INT4, one activation row.  Block q goes through its own accumulator
+        // and only column q of it is read; columns are independent dot
+        // products, so the other columns may hold anything.  Lane (g, t)
+        // therefore supplies block g & 3's activations for every block: one
+        // set of four 16-byte loads per item, no zero region.  The staged
+        // layout is [chunk][word w][block][lane t] (16 bytes each), so the 16
+        // distinct entries a warp reads for one w are 256 contiguous bytes.
+        static_assert(Fmt::kAcc == kMmaChunkBlocks, "one accumulator per block");
+        const uint4* xb = xs + (lb0 >> 2) * 64 + (gq & 3) * 4 + t;
+        float acc[kMmaChunkBlocks][4];
+#pragma unroll
+        for (int q = 0; q < kMmaChunkBlocks; ++q)
+            acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint4 bb = xb[16 * w];  // (x0,x4) (x1,x5) (x2,x6) (x3,x7) of word w
+#pragma unroll
+            for (int q = 0; q < kMmaChunkBlocks; ++q) {
+                const uint32_t ua = w == 0 ? r.wa[q].x : w == 1 ? r.wa[q].y
+                                                     : w == 2 ? r.wa[q].z : r.wa[q].w;
+                const uint32_t ub = w == 0 ? r.wb[q].x : w == 1 ? r.wb[q].y
+                                                     : w == 2 ? r.wb[q].z : r.wb[q].w;
+                const uint32_t ha = ua >> 8, hb = ub >> 8;
+                mma_16816(acc[q], nib_pair_lo(ua), nib_pair_lo(ub), nib_pair_hi(ua),
+                          nib_pair_hi(ub), bb.x, bb.y);
+                mma_16816(acc[q], nib_pair_lo(ha), nib_pair_lo(hb), nib_pair_hi(ha),
+                          nib_pair_hi(hb), bb.z, bb.w);
+            }
+        }
+        // lane t < 2 holds columns 2t, 2t + 1: blocks 0 / 1 (t = 0) or 2 / 3
+        // (t = 1).  (These are the values the zero-column form summed with
+        // exact zeros; the segment sum below starts from +0, so the results
+        // are the same bits.)
+        const bool odd = (t & 1) != 0;
+        const float e0 = odd ? acc[2][0] : acc[0][0];
+        const float e1 = odd ? acc[3][1] : acc[1][1];
+        const float e2 = odd ? acc[2][2] : acc[0][2];
+        const float e3 = odd ? acc[3][3] : acc[1][3];
+        const float sa0 = scale_at(r.sa, 0), sa1 = scale_at(r.sa, 1);
+        const float sb0 = scale_at(r.sb, 0), sb1 = scale_at(r.sb, 1);
+        sacc.v[0][0] += fmaf(sa1, e1, sa0 * e0);
+        sacc.v[0][1] += fmaf(sb1, e3, sb0 * e2);
+    } else if constexpr (kNB == 0) {
         float acc[Fmt::kAcc][4];
 #pragma unroll
         for (int i = 0; i < Fmt::kAcc; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -730,7 +773,10 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
                     e.y = prmt_i<0x7632u>(v[u].x, v[u].z);
                     e.z = prmt_i<0x5410u>(v[u].y, v[u].w);
                     e.w = prmt_i<0x7632u>(v[u].y, v[u].w);
-                    row[(blk * 4 + w) * 4 + tt] = e;
+                    if constexpr (kNB == 0)  // [chunk][w][block in chunk][lane] (mma_item)
+                        row[(blk >> 2) * 64 + w * 16 + (blk & 3) * 4 + tt] = e;
+                    else
+                        row[(blk * 4 + w) * 4 + tt] = e;
                 } else {
                     row[qs[u]] = v[u];
                 }
