@@ -29,6 +29,7 @@
 #include "gemv_launch.h"
 #include "gemv_vector.cuh"
 #include "gemv_mma.cuh"
+#include "gemv_tc.cuh"
 
 namespace clb {
 
@@ -464,9 +465,28 @@ cudaError_t launch_mma_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream
 //  * several activation rows: one CTA per SM per launch; 4 warps (2..8 rows)
 //    or 16 warps (9..16 rows) for matrices up to 2^25 weights, 8 warps above;
 //    chained or plain launches of 2..8 rows take two 8-warp CTAs per SM.
+cudaError_t launch_tc(const GemvArgs& a, cudaStream_t s, unsigned flags);
+cudaError_t launch_tc_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
+                              unsigned flags);
+
+// INT4 with 9..16 activation rows on few row tiles (fewer than half an SM
+// each, so K is split across a cluster) runs the 5th-generation tensor-core
+// kernel (gemv_tc.cuh), measured faster there than the register-fed kernel
+// (4096 x 4096: 10.2 vs 12.0 us; 8192 x 28672: 67.4 vs 76.1 us); the
+// register-fed kernel keeps the rest (28672 x 8192: 56 vs 73 us).  The choice
+// depends on the shape and the SM count only.
+template <class Fmt>
+bool prefer_tc(const GemvArgs& a) {
+    if (!Fmt::kGroupScale || a.M <= 8) return false;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    return 2 * ((a.N + 127) / 128) < (int64_t)sm_count(dev);
+}
+
 template <class Fmt>
 cudaError_t launch_mma_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
     const bool small = a.N * a.K <= ((int64_t)1 << 25);
+    if (prefer_tc<Fmt>(a)) return launch_tc(a, s, flags);
     if (a.M > 8)
         return small ? launch_mma<Fmt, 16, 1>(a, s, flags) : launch_mma<Fmt, 8, 1>(a, s, flags);
     if (a.M > 1) {
@@ -485,6 +505,7 @@ template <class Fmt>
 cudaError_t launch_mma_sharded_auto(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
                                     unsigned flags) {
     const bool small = a.N * a.K <= ((int64_t)1 << 25);
+    if (prefer_tc<Fmt>(a)) return launch_tc_sharded(a, pa, s, flags);
     if (a.M > 8)
         return small ? launch_mma_sharded<Fmt, 16, 1>(a, pa, s, flags)
                      : launch_mma_sharded<Fmt, 8, 1>(a, pa, s, flags);
@@ -500,8 +521,129 @@ cudaError_t launch_mma_sharded_auto(const GemvArgs& a, const PeerArgs& pa, cudaS
                        : launch_mma_sharded<Fmt, 8, 2>(a, pa, s, flags);
 }
 
+// ---- 5th-generation tensor-core kernel (gemv_tc.cuh) ----
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled, fetched through the runtime (no link-time dependency
+// on the driver library).
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// TMA descriptor of a packed INT4 weight matrix: 2-D {K/2 bytes, N rows},
+// box {128 bytes (two scale groups), 128 rows}, 128-byte swizzle, zero fill
+// past the last row and the row end.  A descriptor depends only on the address
+// and the shape, so
+// it is cached by them (encoding is a host call of about a microsecond).
+cudaError_t int4_weight_map(const void* W, int64_t N, int64_t K, CUtensorMap& out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int64_t, int64_t>, CUtensorMap> cache;
+    const auto key = std::make_tuple(W, N, K);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return cudaSuccess;
+    }
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return cudaErrorNotSupported;
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)(K / 2), (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)(K / 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)(kTcStageGroups * kTcGroupK / 2), (cuuint32_t)kTcRows};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(W), dims, strides,
+                          box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, m);
+    out = m;
+    return cudaSuccess;
+}
+
+// Geometry: one CTA per (128-row tile, K split).  K is split (a cluster of up
+// to 8 CTAs) while the tiles cannot give every SM two CTAs and each split
+// keeps at least four groups per pipeline half; the split depends on the
+// shape and the SM count only.
+TcGeom make_tc_geom(const GemvArgs& a, int num_sms) {
+    TcGeom g{};
+    g.N = a.N;
+    g.K = a.K;
+    g.x_stride = a.x_stride;
+    g.y_stride = a.y_stride;
+    g.M = (int32_t)a.M;
+    g.groups = (int32_t)(a.K / kTcGroupK);
+    g.wait_cycles = g_wait_budget.load(std::memory_order_relaxed);
+    const int64_t tiles = (a.N + kTcRows - 1) / kTcRows;
+    int64_t S = 1;
+    while (S < kTcMaxSplits && tiles * S < 2 * (int64_t)num_sms && g.groups / (2 * S) >= 4) S *= 2;
+    const int64_t gs = (g.groups + S - 1) / S;
+    g.gsplit = (int32_t)gs;
+    g.splits = (int32_t)((g.groups + gs - 1) / gs);  // no empty split
+    return g;
+}
+
+template <bool kPeer>
+cudaError_t launch_tc_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, const PeerOut& po) {
+    const bool ok = aligned16(a.W) && aligned16(a.x) && (a.x_stride % 8) == 0 &&
+                    a.K % kTcGroupK == 0 && a.M >= 1 && a.M <= kTcN && a.N < ((int64_t)1 << 31);
+    if (!ok) {
+        if constexpr (kPeer) return cudaErrorMisalignedAddress;
+        return per_row<launch_int4_scalar>(a, s, flags);
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const TcGeom g = make_tc_geom(a, sm_count(dev));
+    CUtensorMap map;
+    if ((e = int4_weight_map(a.W, a.N, a.K, map)) != cudaSuccess) return e;
+    auto kernel = gemv_tc_int4_kernel<kPeer>;
+    const int smem = tc_smem_total(g);
+    if ((e = ensure_smem_attr(kernel, dev, smem)) != cudaSuccess) return e;
+    const int64_t tiles = (a.N + kTcRows - 1) / kTcRows;
+    return launch(kernel, dim3((unsigned)(tiles * g.splits)), dim3(kTcThreads), (size_t)smem, s,
+                  flags, g.splits, map, static_cast<const __half*>(a.scale),
+                  static_cast<const __half*>(a.x), static_cast<__half*>(a.y), g, po);
+}
+
+cudaError_t launch_tc(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    return launch_tc_impl<false>(a, s, flags, PeerOut{});
+}
+
+cudaError_t launch_tc_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
+                              unsigned flags) {
+    if (pa.world < 1 || pa.world > kMaxPeers || pa.rank < 0 || pa.rank >= pa.world)
+        return cudaErrorInvalidValue;
+    PeerOut po{};
+    for (int p = 0; p < pa.world; ++p) {
+        po.y[0][p] = static_cast<__half*>(pa.y[0][p]);
+        po.y[1][p] = static_cast<__half*>(pa.y[1][p]);
+        po.flag[p] = pa.flag[p];
+    }
+    po.row0 = pa.row0;
+    po.rank = pa.rank;
+    po.world = pa.world;
+    return launch_tc_impl<true>(a, s, flags, po);
+}
+
 const VariantDesc kInt4Variants[] = {
     {"int4gemv_baseline", per_row<launch_int4_scalar>, false},
+    {"int4gemv_tc", launch_tc, false},
     {"int4gemv_bulk", per_row<launch_vec1<Int4Fmt, MathF16, true>>, false},
     {"int4gemv_bulk_f32x2", per_row<launch_vec1<Int4Fmt, MathF32x2, true>>, false},
     {"int4gemv_ldg", per_row<launch_vec1<Int4Fmt, MathF16, false>>, false},
@@ -565,6 +707,7 @@ cudaError_t launch_gemv_f16_mma(const GemvArgs& a, cudaStream_t s, unsigned flag
 
 const ShardedVariantDesc kInt4Sharded[] = {
     {"int4gemv_mma", launch_mma_sharded_auto<MmaInt4>},
+    {"int4gemv_tc", launch_tc_sharded},
     {"int4gemv_mma_w4", launch_mma_sharded<MmaInt4, 4, 1>},
     {"int4gemv_mma_w8", launch_mma_sharded<MmaInt4, 8, 1>},
     {"int4gemv_mma_w8c2", launch_mma_sharded<MmaInt4, 8, 2>},

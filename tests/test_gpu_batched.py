@@ -21,6 +21,8 @@ pytestmark = pytest.mark.gpu
 MMA4 = ["int4gemv_mma", "int4gemv_mma_w4", "int4gemv_mma_w8", "int4gemv_mma_w8c2",
         "int4gemv_mma_w16"]
 MMA8 = [v.replace("int4gemv", "qgemv") for v in MMA4]
+# the 5th-generation tensor-core kernel (tcgen05, TMEM, TMA); INT4 only
+TC4 = ["int4gemv_tc"]
 
 
 def _x(M, K, seed):
@@ -43,7 +45,7 @@ SHAPES4 = [(4096, 4096, 4), (1000, 1024, 3), (256, 8192, 16), (4096, 1152, 9),
 
 
 @pytest.mark.parametrize("shape", SHAPES4, ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("variant", MMA4)
+@pytest.mark.parametrize("variant", MMA4 + TC4)
 def test_int4_batched_vs_oracle(variant, shape):
     N, K, M = shape
     ext = build("int4gemv")
@@ -123,3 +125,35 @@ def test_batched_rejects():
                 torch.zeros(1024, dtype=torch.float16, device="cuda")):
         with pytest.raises(RuntimeError):
             ext.forward_batched("int4gemv_mma", W, s, bad)
+
+
+@pytest.mark.parametrize("flags", [0, 1, 3, 7])
+@pytest.mark.parametrize("M", [1, 16])
+def test_tc_flags_identical(flags, M):
+    """Launch flags change scheduling only: the tcgen05 kernel's K split (and
+    summation order) depends on the shape and the SM count."""
+    ext = build("int4gemv")
+    W, s, _ = make_w4(1024, 8192, seed=11)
+    X = _x(M, 8192, seed=12).cuda()
+    ref = ext.forward_batched("int4gemv_tc", W, s, X)
+    assert torch.equal(ext.forward_batched("int4gemv_tc", W, s, X, flags=flags), ref)
+    assert nat.device_status(clear=True) == 0
+
+
+def test_tc_misaligned_scales_and_zero_rows():
+    """Scale rows at an odd half offset, a zero weight matrix and zero
+    activation rows: the tcgen05 kernel reads scales one at a time and its
+    results stay inside the bound (zeros exactly)."""
+    ext = build("int4gemv")
+    W, s, _ = make_w4(640, 2048, seed=13)
+    buf = torch.empty(s.numel() + 1, dtype=torch.float16, device="cuda")
+    s2 = buf[1:].view(s.shape)
+    s2.copy_(s)
+    X = _x(5, 2048, seed=14)
+    X[2].zero_()
+    Y = ext.forward_batched("int4gemv_tc", W, s2, X.cuda()).cpu().numpy()
+    _check_rows(o4, Y, W, s, X.numpy())
+    assert not Y[2].any()
+    Z = ext.forward_batched("int4gemv_tc", torch.zeros_like(W), s, X.cuda())
+    assert not Z.any()
+    assert nat.device_status(clear=True) == 0

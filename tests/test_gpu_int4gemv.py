@@ -224,6 +224,28 @@ def test_sharded_fused_single_rank(ext, one_rank_group, variant, flags):
         sg.close()
 
 
+@pytest.mark.parametrize("M", [1, 3, 16])
+@pytest.mark.parametrize("variant", ["int4gemv_tc", "int4gemv_mma"])
+def test_sharded_fused_single_rank_batches(ext, one_rank_group, variant, M):
+    """Several activation rows through the fused sharded step on one rank
+    (the tcgen05 kernel's peer epilogue included; "int4gemv_mma" routes 16
+    rows on few tiles to it) equal the plain batched GEMV bit for bit."""
+    from cudalab_b200.sharded import ShardedGemv
+    Wp, s, _ = make_w4(1000, 4096, seed=5)
+    sg = ShardedGemv("int4gemv", Wp, s, 1000, 4096, variant=variant, mode="fused", max_batch=16)
+    try:
+        for step in range(3):
+            X = torch.randn(M, 4096, generator=torch.Generator().manual_seed(60 + step))
+            X = X.half().cuda()
+            y = sg.forward(X if M > 1 else X[0], flags=3).clone().view(M, 1000)
+            ref = ext.forward_batched(variant, Wp, s, X)
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref), step
+        assert nat.device_status(clear=True) == 0
+    finally:
+        sg.close()
+
+
 @pytest.mark.parametrize("graph", [False, True])
 def test_outputs_free_chain_completes_in_order(ext, graph):
     """A chain of independent GEMVs launched with PDL | INPUTS_READY |
