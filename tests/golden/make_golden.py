@@ -13,6 +13,7 @@ fixtures travel; the reference does not.
 
     python tests/golden/make_golden.py               # all fixtures
     python tests/golden/make_golden.py --only-gemv   # the dense GEMV fixture
+    python tests/golden/make_golden.py --only-rmsnorm  # RMSNorm and fused fixtures
 """
 from __future__ import annotations
 
@@ -99,13 +100,76 @@ def make_gemv() -> None:
     print("wrote", HERE / "gemv_golden.npz")
 
 
+RMSNORM_CASES = [  # (M, H, mode, seed): the reference's RMSNorm on its own generator
+    (1, 4096, "normal", 0),
+    (3, 1024, "tiny", 1),
+    (2, 2048, "biased", 2),
+    (1, 512, "zeros", 3),
+    (4, 8192, "normal", 4),
+]
+FUSED_CASES = [  # (N, K, M, mode, seed_w, seed_x): RMSNorm of x, then the INT4 layer-A
+    (64, 1024, 1, "normal", 0, 1),
+    (16, 4096, 3, "biased", 2, 3),
+    (40, 2048, 2, "tiny", 4, 5),
+]
+
+
+def make_rmsnorm() -> None:
+    """RMSNorm fixtures (cudalab/reference.py:rmsnorm_ref and make_inputs) and
+    fused RMSNorm -> INT4 GEMV fixtures: the reference's RMSNorm output fed
+    to its INT4 layer-A reference and fp64 exact values."""
+    from cudalab.reference import make_inputs, rmsnorm_ref  # reference code
+    from cudalab.operators.gemv import make_w
+    from cudalab import int4gemv_quantize as q4
+
+    out = {}
+    for i, (M, H, mode, seed) in enumerate(RMSNORM_CASES):
+        x, w = make_inputs(M, H, torch.float16, device="cpu", seed=seed, mode=mode)
+        y = rmsnorm_ref(x, w)
+        p = f"c{i}_"
+        out[p + "meta"] = np.array([M, H, seed], np.int64)
+        out[p + "mode"] = np.array(mode)
+        out[p + "x"] = _bits16(x)
+        out[p + "w"] = _bits16(w)
+        out[p + "y_ref"] = _bits16(y)
+    out["n_cases"] = np.array(len(RMSNORM_CASES))
+    out["eps"] = np.array(1e-5)
+    for i, (N, K, M, mode, sw, sx) in enumerate(FUSED_CASES):
+        W = make_w(N, K, torch.float16, device="cpu", seed=sw, mode="normal")
+        Wp, s16 = q4.quantize_w(W)
+        x, g = make_inputs(M, K, torch.float16, device="cpu", seed=sx, mode=mode)
+        xn = rmsnorm_ref(x, g)
+        Wd = q4.dequantize_w(Wp, s16)
+        y_ref = torch.stack([torch.mv(Wd, xn[m].float()) for m in range(M)]).to(torch.float16)
+        a = q4.unpack_w(Wp).double() * s16.double().repeat_interleave(128, dim=1)
+        exact = xn.double() @ a.t()
+        S = xn.double().abs() @ a.abs().t()
+        p = f"f{i}_"
+        out[p + "meta"] = np.array([N, K, M, sw, sx], np.int64)
+        out[p + "W_packed"] = Wp.numpy()
+        out[p + "scale"] = _bits16(s16)
+        out[p + "x"] = _bits16(x)
+        out[p + "g"] = _bits16(g)
+        out[p + "xn_ref"] = _bits16(xn)
+        out[p + "y_ref"] = _bits16(y_ref)
+        out[p + "exact"] = exact.numpy()
+        out[p + "S"] = S.numpy()
+    out["n_fused"] = np.array(len(FUSED_CASES))
+    np.savez_compressed(HERE / "rmsnorm_golden.npz", **out)
+    print("wrote", HERE / "rmsnorm_golden.npz")
+
+
 def main() -> None:
     if not REF.exists():
         raise SystemExit(f"reference tree not found at {REF}; fixtures are committed already")
     sys.path.insert(0, str(REF))
+    if "--only-rmsnorm" in sys.argv:
+        make_rmsnorm()
+        return
     if "--only-gemv" not in sys.argv:
         make_quantized()
     make_gemv()
+    make_rmsnorm()
 
 
 def make_quantized() -> None:
