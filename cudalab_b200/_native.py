@@ -74,6 +74,9 @@ PROTOTYPES = {
     "cl_gemv_native_timing": (_int, [_cs, _vp, _vp, _vp, _i64, _i64, _int, _i64, _i64, _i64, _vp,
                                      _u32, _dp]),
     "cl_gemv_list_variants": (_int, [_int, ctypes.c_char_p, _size, ctypes.POINTER(_size)]),
+    "cl_rmsnorm_f16": (_int, [_vp, _vp, ctypes.c_float, _vp, _i64, _i64, _vp, _u32]),
+    "cl_int4gemv_rmsnorm": (_int, [_cs, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _i64, _i64,
+                                   _i64, _vp, _u32]),
 }
 
 CL_MAX_PEERS = 8

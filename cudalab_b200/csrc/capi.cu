@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -362,6 +363,51 @@ int cl_int4gemv_list_variants(int which, char* buf, size_t buf_len, size_t* need
     int n = 0;
     const clb::VariantDesc* t = clb::int4_variants(&n);
     return list_variants(t, n, which, buf, buf_len, needed);
+}
+
+// ---- RMSNorm and the fused RMSNorm -> INT4 GEMV ----
+int cl_rmsnorm_f16(const void* X, const void* weight, float eps, void* Y, int64_t M, int64_t H,
+                   void* stream, uint32_t flags) {
+    if (M <= 0) return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: M must be > 0");
+    if (H <= 0) return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: H must be > 0");
+    if (H % 8 != 0) return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: H must be a multiple of 8");
+    if (H > 3 * ((int64_t)1 << 20))
+        return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: H exceeds 3 * 2^20 halves");
+    if (M > INT32_MAX) return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: M exceeds 2^31 - 1 rows");
+    if (!(eps >= 0.f) || !std::isfinite(eps))
+        return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: eps must be finite and >= 0");
+    if (!X || !weight || !Y) return fail(CL_ERR_INVALID_ARGUMENT, "rmsnorm: null device pointer");
+    cudaError_t e = clb::launch_rmsnorm_f16(X, weight, eps, Y, M, H,
+                                            static_cast<cudaStream_t>(stream), flags);
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+    return CL_OK;
+}
+
+int cl_int4gemv_rmsnorm(const char* variant, const uint8_t* W_packed, const void* scale,
+                        const void* X, const void* norm_weight, float eps, void* Y, int64_t M,
+                        int64_t N, int64_t K, void* stream, uint32_t flags) {
+    int n = 0;
+    const clb::VariantDesc* t = clb::int4_rmsnorm_variants(&n);
+    const char* op = "int4gemv_rmsnorm";
+    const clb::VariantDesc* v = find(t, n, variant);
+    if (!v) return fail(CL_ERR_UNKNOWN_VARIANT, unknown_msg(op, t, n, variant));
+    if (M <= 0) return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": M must be > 0");
+    const int rc = check_args(op, W_packed, scale, X, Y, N, K, true);
+    if (rc != CL_OK) return rc;
+    if (!norm_weight) return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": null norm weight");
+    if (!(eps >= 0.f) || !std::isfinite(eps))
+        return fail(CL_ERR_INVALID_ARGUMENT, std::string(op) + ": eps must be finite and >= 0");
+    constexpr int64_t kPass = 16;
+    for (int64_t m0 = 0; m0 < M; m0 += kPass) {
+        clb::GemvArgs a{W_packed, scale, static_cast<const uint16_t*>(X) + m0 * K,
+                        static_cast<uint16_t*>(Y) + m0 * N, N, K,
+                        std::min<int64_t>(kPass, M - m0), K, N};
+        a.norm_w = norm_weight;
+        a.norm_eps = eps;
+        cudaError_t e = v->fn(a, static_cast<cudaStream_t>(stream), flags);
+        if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    }
+    return CL_OK;
 }
 
 // ---- INT8 ----

@@ -269,9 +269,10 @@ cudaError_t per_row(const GemvArgs& a, cudaStream_t s, unsigned flags) {
 //   budget; the row groups then target SMs x ctas_per_sm CTAs (1 for 8-warp
 //   CTAs, 2 for a shorter per-launch latency), capped by max_groups (clusters
 //   that can be resident at once).  Returns false when no split fits in
-//   shared memory.
+//   shared memory.  `norm`: room for the fused RMSNorm's unit sums (the split
+//   and every other choice stay those of the plain launch).
 bool make_mma_geom(int64_t N, int64_t K, int64_t M, int kind, int num_sms, int ctas_per_sm,
-                   int64_t max_groups, MmaGeom& g) {
+                   int64_t max_groups, MmaGeom& g, bool norm = false) {
     g = MmaGeom{};
     g.wait_cycles = g_wait_budget.load(std::memory_order_relaxed);
     g.N = N;
@@ -328,6 +329,11 @@ bool make_mma_geom(int64_t N, int64_t K, int64_t M, int kind, int num_sms, int c
     const int64_t rt = std::max<int64_t>(1, std::min<int64_t>(max_tiles, part_budget / per_tile));
     g.round_tiles = (int32_t)rt;
     g.part_floats = (int32_t)(rt * n_seg * 16 * M);
+    // fused RMSNorm unit sums: of the whole row (one row), of this split's
+    // part of every row (several rows)
+    if (norm)
+        g.norm_units = (int32_t)(M == 1 ? (K + kNormUnitHalves - 1) / kNormUnitHalves
+                                        : kc_split * kMmaChunkBlocks * bw / kNormUnitWords);
     return mma_smem_total(g) <= 226 * 1024;  // 1 KiB left for static shared memory
 }
 
@@ -353,20 +359,23 @@ cudaError_t max_active_clusters(K kernel, const cudaLaunchConfig_t& cfg, int dev
 
 // Launch of one tensor-core GEMV (kNB from M).  Peer mode: rows go to every
 // rank's buffers (`po`); the sharded entry points check the contract first.
-template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer>
+// kNorm: fused RMSNorm of the activation rows (a.norm_w, a.norm_eps); no
+// scalar fallback (an unmet contract is an error).
+template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer, bool kNorm = false>
 cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, const PeerOut& po) {
     constexpr bool kInt4 = Fmt::kGroupScale;
     const bool ok = aligned16(a.W) && aligned16(a.x) && (a.x_stride % 8) == 0 &&
                     a.K % Fmt::kKAlign == 0 && a.M >= 1 &&
-                    a.M <= kMmaMaxM;
+                    a.M <= kMmaMaxM && (!kNorm || aligned16(a.norm_w));
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     MmaGeom g;
     const bool geom =
-        ok && make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, 0, g);
+        ok && make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, 0, g, kNorm);
     if (!geom) {
-        if constexpr (kPeer) return ok ? cudaErrorInvalidConfiguration : cudaErrorMisalignedAddress;
+        if constexpr (kPeer || kNorm)
+            return ok ? cudaErrorInvalidConfiguration : cudaErrorMisalignedAddress;
         return per_row<Fmt::kKind == MmaInt4::kKind   ? launch_int4_scalar
                        : Fmt::kKind == MmaInt8::kKind ? launch_int8_scalar
                                                       : launch_f16_scalar>(a, s, flags);
@@ -406,7 +415,7 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
                 const int64_t x_stride = g.x_stride, y_stride = g.y_stride;
                 const int early = g.early_x, free_y = g.free_y;
                 if (!make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, clusters,
-                                   g))
+                                   g, kNorm))
                     return cudaErrorInvalidConfiguration;
                 g.x_stride = x_stride;
                 g.y_stride = y_stride;
@@ -416,26 +425,33 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
                 if ((err = ensure_smem_attr(kernel, dev, smem)) != cudaSuccess) return err;
             }
         }
+        g.norm_w = static_cast<const __half*>(a.norm_w);
+        g.norm_eps = a.norm_eps;
         return launch(kernel, dim3((unsigned)(g.groups * g.splits)), dim3(32 * kWarps),
                       (size_t)smem, s, flags, g.splits, static_cast<const uint8_t*>(a.W),
                       static_cast<const S*>(a.scale), static_cast<const __half*>(a.x),
                       static_cast<__half*>(a.y), g, po);
     };
     if (a.M == 1) {
-        return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 0, true, kPeer>)
-                        : go(gemv_mma_kernel<Fmt, kWarps, 0, false, kPeer>);
+        return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 0, true, kPeer, kNorm>)
+                        : go(gemv_mma_kernel<Fmt, kWarps, 0, false, kPeer, kNorm>);
     }
     if (a.M <= 8) {
-        return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 1, true, kPeer>)
-                        : go(gemv_mma_kernel<Fmt, kWarps, 1, false, kPeer>);
+        return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 1, true, kPeer, kNorm>)
+                        : go(gemv_mma_kernel<Fmt, kWarps, 1, false, kPeer, kNorm>);
     }
-    return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 2, true, kPeer>)
-                    : go(gemv_mma_kernel<Fmt, kWarps, 2, false, kPeer>);
+    return all_full ? go(gemv_mma_kernel<Fmt, kWarps, 2, true, kPeer, kNorm>)
+                    : go(gemv_mma_kernel<Fmt, kWarps, 2, false, kPeer, kNorm>);
 }
 
 template <class Fmt, int kWarps, int kCtasPerSm>
 cudaError_t launch_mma(const GemvArgs& a, cudaStream_t s, unsigned flags) {
     return launch_mma_impl<Fmt, kWarps, kCtasPerSm, false>(a, s, flags, PeerOut{});
+}
+
+template <int kWarps, int kCtasPerSm>
+cudaError_t launch_mma_norm(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    return launch_mma_impl<MmaInt4, kWarps, kCtasPerSm, false, true>(a, s, flags, PeerOut{});
 }
 
 template <class Fmt, int kWarps, int kCtasPerSm>
@@ -499,6 +515,53 @@ cudaError_t launch_mma_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
                             : launch_mma<Fmt, 8, 1>(a, s, flags);
     }
     return a.K <= 2048 ? launch_mma<Fmt, 8, 1>(a, s, flags) : launch_mma<Fmt, 8, 2>(a, s, flags);
+}
+
+// Fused RMSNorm -> INT4 GEMV: the geometry of launch_mma_auto, with the
+// register-fed kernel also for 9..16 rows on few row tiles.
+cudaError_t launch_mma_norm_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
+    const bool small = a.N * a.K <= ((int64_t)1 << 25);
+    if (a.M > 8) return small ? launch_mma_norm<16, 1>(a, s, flags) : launch_mma_norm<8, 1>(a, s, flags);
+    if (a.M > 1) {
+        if ((flags & 3u) != 3u) return launch_mma_norm<8, 2>(a, s, flags);
+        return small ? launch_mma_norm<4, 1>(a, s, flags) : launch_mma_norm<8, 1>(a, s, flags);
+    }
+    if ((flags & 3u) == 3u) {
+        if (a.K <= 4096) return launch_mma_norm<2, 1>(a, s, flags);
+        return a.K <= 16384 ? launch_mma_norm<4, 1>(a, s, flags) : launch_mma_norm<8, 1>(a, s, flags);
+    }
+    return a.K <= 2048 ? launch_mma_norm<8, 1>(a, s, flags) : launch_mma_norm<8, 2>(a, s, flags);
+}
+
+// Standalone RMSNorm: one 256-thread CTA per row.  The sum of squares in the
+// order of the fused kernel (row_unit_sums, row_sum_of_units in gemv_mma.cuh),
+// then every 16-byte word normalised.
+constexpr int kRmsThreads = 256;
+constexpr int kRmsMaxUnits = 12288;  // 48 KiB of unit sums: H <= 3 Mi halves
+
+__global__ void __launch_bounds__(kRmsThreads)
+rmsnorm_f16_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
+                   __half* __restrict__ y, int64_t H, float eps) {
+    extern __shared__ float s_units[];
+    __shared__ float s_r;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    const int64_t row = blockIdx.x;
+    row_unit_sums<kRmsThreads / 32>(x + row * H, H, s_units);
+    __syncthreads();
+    if (warp == 0) {
+        const float s =
+            row_sum_of_units(s_units, (int)((H + kNormUnitHalves - 1) / kNormUnitHalves), lane);
+        if (lane == 0) s_r = inv_rms(s, H, eps);
+    }
+    __syncthreads();
+    const float r = s_r;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * H);
+    const uint4* wr = reinterpret_cast<const uint4*>(w);
+    uint4* yr = reinterpret_cast<uint4*>(y + row * H);
+    for (int64_t q = threadIdx.x; q < H / 8; q += kRmsThreads)
+        yr[q] = norm_word(__ldg(xr + q), __ldg(wr + q), r);
 }
 
 template <class Fmt>
@@ -699,7 +762,34 @@ const VariantDesc kInt8Variants[] = {
     {"qgemv_warp_vec16_ilp4", per_row<launch_vec1<Int8Fmt, MathF16, true>>, false},
 };
 
+// Fused RMSNorm -> INT4 GEMV: the dispatch and fixed geometries (identical
+// results: the normalised activations do not depend on the block size).
+const VariantDesc kInt4NormVariants[] = {
+    {"int4gemv_rmsnorm", launch_mma_norm_auto, false},
+    {"int4gemv_rmsnorm_w2", launch_mma_norm<2, 1>, false},
+    {"int4gemv_rmsnorm_w4", launch_mma_norm<4, 1>, false},
+    {"int4gemv_rmsnorm_w8", launch_mma_norm<8, 1>, false},
+    {"int4gemv_rmsnorm_w8c2", launch_mma_norm<8, 2>, false},
+    {"int4gemv_rmsnorm_w16", launch_mma_norm<16, 1>, false},
+};
+
 }  // namespace
+
+const VariantDesc* int4_rmsnorm_variants(int* count) {
+    *count = (int)(sizeof(kInt4NormVariants) / sizeof(kInt4NormVariants[0]));
+    return kInt4NormVariants;
+}
+
+cudaError_t launch_rmsnorm_f16(const void* x, const void* w, float eps, void* y, int64_t M,
+                               int64_t H, cudaStream_t s, unsigned flags) {
+    if (M <= 0 || H <= 0 || H % 8 != 0 || M > INT32_MAX) return cudaErrorInvalidValue;
+    const int64_t units = (H + kNormUnitHalves - 1) / kNormUnitHalves;
+    if (units > kRmsMaxUnits) return cudaErrorInvalidValue;
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return cudaErrorMisalignedAddress;
+    return launch(rmsnorm_f16_kernel, dim3((unsigned)M), dim3(kRmsThreads), (size_t)units * 4, s,
+                  flags, 1, static_cast<const __half*>(x), static_cast<const __half*>(w),
+                  static_cast<__half*>(y), H, eps);
+}
 
 cudaError_t launch_gemv_f16_mma(const GemvArgs& a, cudaStream_t s, unsigned flags) {
     return launch_mma_auto<MmaF16>(a, s, flags);

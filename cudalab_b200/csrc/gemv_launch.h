@@ -13,6 +13,8 @@ namespace clb {
 // or unused (dense); x holds M activation rows of
 // K halves (x_stride halves apart), y receives M rows of N halves (y_stride
 // apart; in peer mode, rows of the full matrix in every rank's buffer).
+// norm_w / norm_eps: RMSNorm weight (K halves, 16-byte aligned) and epsilon
+// of the fused RMSNorm -> GEMV launches; unused elsewhere.
 struct GemvArgs {
     const void* W;
     const void* scale;
@@ -20,6 +22,8 @@ struct GemvArgs {
     void* y;
     int64_t N, K, M;
     int64_t x_stride, y_stride;
+    const void* norm_w = nullptr;
+    float norm_eps = 0.f;
 };
 
 // flags are the CL_LAUNCH_* bits of the public header.
@@ -51,6 +55,11 @@ struct ShardedVariantDesc {
 
 const VariantDesc* int4_variants(int* count);
 const VariantDesc* int8_variants(int* count);
+// Fused RMSNorm -> INT4 GEMV (GemvArgs.norm_w / norm_eps set; x_stride == K).
+const VariantDesc* int4_rmsnorm_variants(int* count);
+// Standalone RMSNorm of M fp16 rows of H halves (H % 8 == 0, 16-byte aligned).
+cudaError_t launch_rmsnorm_f16(const void* x, const void* w, float eps, void* y, int64_t M,
+                               int64_t H, cudaStream_t stream, unsigned flags);
 const ShardedVariantDesc* int4_sharded_variants(int* count);
 const ShardedVariantDesc* int8_sharded_variants(int* count);
 

@@ -80,12 +80,15 @@ struct MmaGeom {
     int32_t early_x;              // x is not written by the preceding kernel
     int32_t free_y;               // y is not accessed by any kernel still in flight
     long long wait_cycles;        // bound of the peer-flag wait (SM cycles)
+    const __half* norm_w;         // RMSNorm weight [K] (fused-prologue kernels)
+    float norm_eps;
+    int32_t norm_units;           // RMSNorm unit sums per row of one split (0: no RMSNorm)
 };
 
 constexpr int kZeroRegion = 256;  // bytes of zeros ahead of the staged activations
 
 // Shared memory: [zeros | activations | item partials | INT8 row scales |
-// row sums of this split (splits > 1)]
+// row sums of this split (splits > 1) | RMSNorm unit sums (fused RMSNorm)]
 __host__ __device__ inline int mma_xs_off() { return kZeroRegion; }
 __host__ __device__ inline int mma_part_off(const MmaGeom& g) {
     return kZeroRegion + g.M * g.xs_words * 16;
@@ -96,8 +99,11 @@ __host__ __device__ inline int mma_sc_off(const MmaGeom& g) {
 __host__ __device__ inline int mma_rsum_off(const MmaGeom& g) {
     return mma_sc_off(g) + ((g.max_rows * 4 + 15) & ~15);
 }
-__host__ __device__ inline int mma_smem_total(const MmaGeom& g) {
+__host__ __device__ inline int mma_unit_off(const MmaGeom& g) {
     return mma_rsum_off(g) + (g.splits > 1 ? g.max_rows * g.M * 4 : 0);
+}
+__host__ __device__ inline int mma_smem_total(const MmaGeom& g) {
+    return mma_unit_off(g) + g.M * g.norm_units * 4;
 }
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -631,6 +637,123 @@ __device__ __forceinline__ void seg_normalize(MmaSegCursor& c, int n_seg) {
 }
 
 // ---------------------------------------------------------------------------
+// RMSNorm of activation rows (the fused prologue and the standalone kernel).
+//
+// Formula of the reference (cudalab/reference.py:41-45, kernels/rmsnorm/
+// rmsnorm_v4.cu:84-108): v = mean(x^2) in fp32, r = 1 / sqrt(v + eps),
+// y = fp16((x * r) * w), each product rounded to fp32.  r is taken correctly
+// rounded here (the reference's rsqrtf is within 2 ulp of it).
+//
+// The fp32 sum of squares has one fixed order, shared by the fused kernel
+// (whatever its geometry and K split) and the standalone kernel, so both
+// produce the same r bit for bit:
+//   word partial  the 8 squares of a 16-byte word: even and odd elements in
+//                 two fp32 lanes (fma, element order), then even + odd;
+//   unit sum      the 32 word partials of a unit (256 halves starting at a
+//                 multiple of 256) added by an xor butterfly (16, 8, 4, 2, 1);
+//   row sum       lane l of a warp adds units l, l + 32, ... in order, then an
+//                 xor butterfly over the 32 lanes.
+// Words past the row end count as zeros (adding +0 changes no bits).  A unit
+// is what one warp of the staging loop holds at once, so the fused kernel
+// takes the unit sums from the words it stages, and a K split exchanges them
+// through distributed shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kNormUnitWords = 32;  // 16-byte words per unit
+constexpr int kNormUnitHalves = 8 * kNormUnitWords;
+
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+    return ((unsigned long long)__float_as_uint(v.y) << 32) | __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 bits_f2(unsigned long long b) {
+    return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
+}
+__device__ __forceinline__ unsigned long long h2_f2_bits(uint32_t h) {
+    return f2_bits(__half22float2(*reinterpret_cast<const __half2*>(&h)));
+}
+
+// Word partial of a 16-byte word of halves.
+__device__ __forceinline__ float sq_word(const uint4& v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    unsigned long long acc = 0ull;  // (+0, +0)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const unsigned long long f = h2_f2_bits(w[i]);
+        asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(acc) : "l"(f));
+    }
+    const float2 a = bits_f2(acc);
+    return a.x + a.y;
+}
+
+__device__ __forceinline__ float warp_xor_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+__device__ __forceinline__ float inv_rms(float sum_sq, int64_t K, float eps) {
+    return __frsqrt_rn(__fdiv_rn(sum_sq, (float)K) + eps);
+}
+
+// Unit sums of one row of K halves (16-byte aligned) into s_unit[0 ..
+// ceil(K / 256)), by a block of kWarps warps: warp w takes units w, w + kWarps,
+// ..., four at a time (loads first, then the four butterflies interleaved).
+template <int kWarps>
+__device__ __forceinline__ void row_unit_sums(const __half* __restrict__ row, int64_t K,
+                                              float* s_unit) {
+    constexpr int kBatch = 4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t words = K / 8;
+    const int n_units = (int)((K + kNormUnitHalves - 1) / kNormUnitHalves);
+    const uint4* p = reinterpret_cast<const uint4*>(row);
+    for (int u0 = warp; u0 < n_units; u0 += kWarps * kBatch) {
+        uint4 v[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int64_t q = (int64_t)(u0 + b * kWarps) * kNormUnitWords + lane;
+            v[b] = q < words ? __ldg(p + q) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        float su[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) su[b] = sq_word(v[b]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) su[b] += __shfl_xor_sync(0xffffffffu, su[b], off);
+        if (lane == 0) {
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b)
+                if (u0 + b * kWarps < n_units) s_unit[u0 + b * kWarps] = su[b];
+        }
+    }
+}
+
+// Row sum from its unit sums (one warp; every lane returns it).
+__device__ __forceinline__ float row_sum_of_units(const float* s_unit, int n_units, int lane) {
+    float s = 0.f;
+    for (int u = lane; u < n_units; u += 32) s += s_unit[u];
+    return warp_xor_sum(s);
+}
+
+// fp16((x * r) * w) of the 8 halves of one 16-byte word: both products
+// rounded to fp32 (packed multiplies, one rounding per element), then to
+// fp16.  Elementwise, so x and w may be permuted alike.
+__device__ __forceinline__ uint4 norm_word(const uint4& xv, const uint4& wv, float r) {
+    const uint32_t xi[4] = {xv.x, xv.y, xv.z, xv.w};
+    const uint32_t wi[4] = {wv.x, wv.y, wv.z, wv.w};
+    const unsigned long long rr = f2_bits(make_float2(r, r));
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        unsigned long long t;
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(h2_f2_bits(xi[i])), "l"(rr));
+        asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(h2_f2_bits(wi[i])));
+        const float2 p = bits_f2(t);
+        o[i] = h2_as_u32(__floats2half2_rn(p.x, p.y));
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
 
@@ -638,7 +761,9 @@ __device__ __forceinline__ void seg_normalize(MmaSegCursor& c, int n_seg) {
 // kernels' CTAs under programmatic dependent launch).  kNB = 2: one CTA per
 // SM (more registers for the second column block).
 // kPeer: y is ignored; rows go to every rank's buffer in `po` (see PeerOut).
-template <class Fmt, int kWarps, int kNB, bool kAllFull, bool kPeer>
+// kNorm: the activation rows are RMSNorm'ed (g.norm_w, g.norm_eps) as they
+// are staged.
+template <class Fmt, int kWarps, int kNB, bool kAllFull, bool kPeer, bool kNorm = false>
 __global__ void __launch_bounds__(32 * kWarps, kNB <= 1 ? 16 / kWarps : 1)
 gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __restrict__ scale,
                 const __half* __restrict__ x, __half* __restrict__ y, const MmaGeom g,
@@ -727,18 +852,81 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     }
     if (tid < kZeroRegion / 4) reinterpret_cast<uint32_t*>(smem)[tid] = 0u;
 
+    // Activations of this split: INT4 in the permuted step order, INT8 as is,
+    // zeros from the row end to the end of the last chunk.
+    const int valid = lblocks * Fmt::kBlockWords;
+    const int words = n_kc * kMmaChunkBlocks * Fmt::kBlockWords;
+    const int64_t k_first = (int64_t)kMmaChunkBlocks * kc0 * Fmt::kBlockWords * 8;
+    // word q of a row: its place in the staged row, and its halves in that order
+    auto stage_at = [&](int qq) -> int {
+        if constexpr (Fmt::kGroupScale) {
+            const int blk = qq >> 4, tt = (qq >> 2) & 3, w = qq & 3;
+            if constexpr (kNB == 0)  // [chunk][w][block in chunk][lane] (mma_item)
+                return (blk >> 2) * 64 + w * 16 + (blk & 3) * 4 + tt;
+            else
+                return (blk * 4 + w) * 4 + tt;
+        } else {
+            return qq;
+        }
+    };
+    auto stage_order = [&](const uint4& v) -> uint4 {
+        if constexpr (Fmt::kGroupScale) {
+            // entry (blk, w, tt): step 2w (x0, x4, x1, x5), step 2w+1 (x2, x6, x3, x7)
+            uint4 e;
+            e.x = prmt_i<0x5410u>(v.x, v.z);
+            e.y = prmt_i<0x7632u>(v.x, v.z);
+            e.z = prmt_i<0x5410u>(v.y, v.w);
+            e.w = prmt_i<0x7632u>(v.y, v.w);
+            return e;
+        } else {
+            return v;
+        }
+    };
+    // Fused RMSNorm.  One activation row (kNB = 0): the row's unit sums are
+    // taken first, straight from global memory, and the staging loop then
+    // normalises in registers (the norm weight words loaded beside x).
+    // Several rows: the staging loop takes the unit sums of the words it
+    // holds (the 32 lanes of a warp hold one unit of one row at a time: words
+    // is a multiple of 32), a K split exchanges them through distributed
+    // shared memory, and a pass over the staged words normalises them in
+    // place, walking words q = tid, tid + kThreads, ... of the norm weight
+    // (kNormBatch loads in flight) and applying each to every row.  The norm
+    // weight, like W, is never written by the preceding kernel.
+    constexpr bool kNormRow = kNorm && kNB == 0;
+    constexpr bool kNormRows = kNorm && kNB != 0;
+    constexpr int kNormBatch = !kNormRows ? 1 : (kNB == 1 || kWarps > 8) ? 4 : 8;  // registers
+    static_assert(!kNorm || (kMmaChunkBlocks * Fmt::kBlockWords) % kNormUnitWords == 0,
+                  "a chunk is whole RMSNorm units");
+    float* s_unit = reinterpret_cast<float*>(smem + mma_unit_off(g));
+    __shared__ float s_inv[kNorm ? kMmaMaxM : 1];
+    const int n_units = (int)((g.K + kNormUnitHalves - 1) / kNormUnitHalves);
+    uint4 nw[kNormBatch];
+    const uint4* nw_src = reinterpret_cast<const uint4*>(g.norm_w + k_first);
+    auto load_norm_w = [&](int qb) {
+#pragma unroll
+        for (int b = 0; b < kNormBatch; ++b) {
+            const int q = qb + b * kThreads;
+            nw[b] = q < valid ? __ldg(nw_src + q) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+
     // Without the caller's promise that x is not produced by the preceding
     // kernel, x may only be read after that kernel has completed.
     if (!g.early_x) pdl_wait_prior_grids();
-    // Activations of this split: INT4 in the permuted step order, INT8 as is,
-    // zeros from the row end to the end of the last chunk.  (row m, word q)
-    // pairs are walked in order, kStageBatch loads in flight per thread before
-    // their stores.
+    if constexpr (kNormRow) {
+        row_unit_sums<kWarps>(x, g.K, s_unit);
+        __syncthreads();
+        if (warp == 0) {
+            const float s = row_sum_of_units(s_unit, n_units, lane);
+            if (lane == 0) s_inv[0] = inv_rms(s, g.K, g.norm_eps);
+        }
+        __syncthreads();
+    }
+    // (row m, word q) pairs are walked in order, kStageBatch loads in flight
+    // per thread before their stores.
+    constexpr int kStageBatch = 4;
     {
-        constexpr int kStageBatch = 4;
-        const int valid = lblocks * Fmt::kBlockWords;
-        const int words = n_kc * kMmaChunkBlocks * Fmt::kBlockWords;
-        const int64_t k_first = (int64_t)kMmaChunkBlocks * kc0 * Fmt::kBlockWords * 8;
+        const float r_row = kNormRow ? s_inv[0] : 0.f;
         int m = 0, q = tid;
         while (m < M && q >= words) {
             q -= words;
@@ -746,44 +934,80 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
         }
         while (m < M) {
             uint4 v[kStageBatch];
+            uint4 vw[kNormRow ? kStageBatch : 1];
             int qs[kStageBatch], ms[kStageBatch];
 #pragma unroll
             for (int u = 0; u < kStageBatch; ++u) {
                 ms[u] = m;
                 qs[u] = q;
                 v[u] = make_uint4(0u, 0u, 0u, 0u);
-                if (m < M && q < valid)
+                if (m < M && q < valid) {
                     v[u] = __ldg(reinterpret_cast<const uint4*>(x + m * g.x_stride + k_first) + q);
+                    if constexpr (kNormRow) vw[u] = __ldg(nw_src + q);
+                }
                 q += kThreads;
                 while (m < M && q >= words) {
                     q -= words;
                     ++m;
                 }
             }
+            if constexpr (kNormRows) {
+                // the batch's unit sums, butterflies interleaved (words past
+                // the last row are zeros; their sums are not stored)
+                float su[kStageBatch];
+#pragma unroll
+                for (int u = 0; u < kStageBatch; ++u) su[u] = sq_word(v[u]);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                    for (int u = 0; u < kStageBatch; ++u)
+                        su[u] += __shfl_xor_sync(0xffffffffu, su[u], off);
+                if (lane == 0) {
+#pragma unroll
+                    for (int u = 0; u < kStageBatch; ++u)
+                        if (ms[u] < M) s_unit[ms[u] * g.norm_units + (qs[u] >> 5)] = su[u];
+                }
+            }
 #pragma unroll
             for (int u = 0; u < kStageBatch; ++u) {
-                if (ms[u] >= M) break;
-                uint4* row = xs4 + ms[u] * g.xs_words;
-                if constexpr (Fmt::kGroupScale) {
-                    const int qq = qs[u];
-                    const int blk = qq >> 4, tt = (qq >> 2) & 3, w = qq & 3;
-                    // entry (blk, w, tt): step 2w (x0, x4, x1, x5), step 2w+1 (x2, x6, x3, x7)
-                    uint4 e;
-                    e.x = prmt_i<0x5410u>(v[u].x, v[u].z);
-                    e.y = prmt_i<0x7632u>(v[u].x, v[u].z);
-                    e.z = prmt_i<0x5410u>(v[u].y, v[u].w);
-                    e.w = prmt_i<0x7632u>(v[u].y, v[u].w);
-                    if constexpr (kNB == 0)  // [chunk][w][block in chunk][lane] (mma_item)
-                        row[(blk >> 2) * 64 + w * 16 + (blk & 3) * 4 + tt] = e;
-                    else
-                        row[(blk * 4 + w) * 4 + tt] = e;
-                } else {
-                    row[qs[u]] = v[u];
+                if (ms[u] >= M) break;  // uniform across the warp
+                if constexpr (kNormRow) {
+                    if (qs[u] < valid) v[u] = norm_word(v[u], vw[u], r_row);
                 }
+                xs4[ms[u] * g.xs_words + stage_at(qs[u])] = stage_order(v[u]);
             }
         }
     }
+    if constexpr (kNormRows) load_norm_w(tid);
     __syncthreads();
+    if constexpr (kNormRows) {
+        // 1 / RMS of every row from all its unit sums (every split's, in
+        // order), then the staged words normalised in place.
+        if (g.splits > 1) cluster_sync_all();
+        for (int m = warp; m < M; m += kWarps) {
+            float s = 0.f;
+            for (int u = lane; u < n_units; u += 32) {
+                const int sp = u / g.norm_units;
+                const float* a = s_unit + m * g.norm_units + (u - sp * g.norm_units);
+                s += g.splits > 1 ? ld_cluster_f32(a, (uint32_t)sp) : *a;
+            }
+            s = warp_xor_sum(s);
+            if (lane == 0) s_inv[m] = inv_rms(s, g.K, g.norm_eps);
+        }
+        __syncthreads();
+        for (int qb = tid; qb < valid; qb += kNormBatch * kThreads) {
+            if (qb != tid) load_norm_w(qb);
+#pragma unroll
+            for (int b = 0; b < kNormBatch; ++b) {
+                const int q = qb + b * kThreads;
+                if (q >= valid) break;
+                const uint4 wq = stage_order(nw[b]);
+                uint4* e = xs4 + stage_at(q);
+                for (int m = 0; m < M; ++m, e += g.xs_words) *e = norm_word(*e, wq, s_inv[m]);
+            }
+        }
+        __syncthreads();
+    }
 
     const uint4* zero4 = reinterpret_cast<const uint4*>(smem);
     const int RT = g.round_tiles;

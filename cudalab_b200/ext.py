@@ -258,6 +258,49 @@ class Int4gemvExt(_ExtBase):
     def _k_of(self, W) -> int:
         return 2 * W.size(1)
 
+    # ---- fused RMSNorm -> INT4 GEMV (no reference counterpart; English messages) ----
+    def rmsnorm_variants(self) -> list[str]:
+        return ["int4gemv_rmsnorm", "int4gemv_rmsnorm_w2", "int4gemv_rmsnorm_w4",
+                "int4gemv_rmsnorm_w8", "int4gemv_rmsnorm_w8c2", "int4gemv_rmsnorm_w16"]
+
+    def forward_rmsnorm(self, variant: str, W_packed, scale, X, norm_weight, eps: float = 1e-5,
+                        out=None, flags: int = 0) -> torch.Tensor:
+        """Y = W * RMSNorm(X, norm_weight) per row of X ([M, K] -> [M, N], or
+        [K] -> [N]) in one launch per 16 rows; equal bit for bit to rmsnorm()
+        followed by forward_batched(variant 'int4gemv_mma_w8c2')."""
+        _chk(variant in self.rmsnorm_variants(),
+             f"unknown int4gemv_rmsnorm variant '{variant}'; available: "
+             f"{' '.join(self.rmsnorm_variants())}")
+        self._validate_w(W_packed)
+        self._validate_scale(W_packed, scale)
+        K, N = self._k_of(W_packed), W_packed.size(0)
+        X2 = X.unsqueeze(0) if X.dim() == 1 else X
+        M = self._validate_batch(W_packed, X2, K)
+        _chk(norm_weight.dim() == 1 and norm_weight.size(0) == K,
+             f"norm_weight must be 1-D of length K={K}")
+        _chk(norm_weight.dtype == torch.float16 and norm_weight.is_contiguous(),
+             "norm_weight must be contiguous float16")
+        _chk(norm_weight.is_cuda and norm_weight.device == W_packed.device,
+             "norm_weight must be on the device of W_packed")
+        _chk(eps >= 0.0 and eps == eps and eps != float("inf"), "eps must be finite and >= 0")
+        shape = (N,) if X.dim() == 1 else (M, N)
+        if out is None:
+            out = torch.empty(shape, dtype=torch.float16, device=W_packed.device)
+        else:
+            _chk(tuple(out.shape) == shape and out.dtype == torch.float16 and out.is_contiguous()
+                 and out.is_cuda and out.device == W_packed.device,
+                 f"out must be contiguous float16 {list(shape)} on the device of W_packed")
+        dev = W_packed.device
+        with torch.cuda.device(dev):
+            rc = self._lib.cl_int4gemv_rmsnorm(
+                variant.encode(), W_packed.data_ptr(), scale.data_ptr(), X2.data_ptr(),
+                norm_weight.data_ptr(), float(eps), out.data_ptr(), M, N, K, _stream_ptr(dev),
+                flags)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"int4gemv_rmsnorm launch failed ({rc}): "
+                               f"{nat.last_error(self._lib)}")
+        return out
+
     @staticmethod
     def _fast_inputs(Wp, scale, x) -> bool:
         if Wp.dtype is not _U8 or Wp.dim() != 2 or not Wp.is_contiguous():
@@ -469,7 +512,67 @@ class GemvExt:
         return timing_result(variant, warmup, n_windows, launches_per_window, buf)
 
 
-_EXT_TYPES = {"int4gemv": Int4gemvExt, "qgemv": QgemvExt, "gemv": GemvExt}
+class RmsnormExt:
+    """fp16 RMSNorm: mirrors `forward` / `forward_into` / `variants` of
+    kernels/rmsnorm/bindings.cpp:91-115 (argument names and the checks of
+    validate_common, :24-41) for the one kernel here, registered as
+    'rmsnorm_f16'.  fp32 rows are not supported (RuntimeError); H must be a
+    multiple of 8."""
+    kind = "rmsnorm"
+
+    def __init__(self) -> None:
+        self._lib = nat.load()
+
+    def variants(self) -> list[str]:
+        return ["rmsnorm_f16"]
+
+    def _validate(self, variant: str, x, w, eps: float) -> None:
+        _chk(variant in self.variants(),
+             f"未知 rmsnorm 变体 '{variant}'。可用: rmsnorm_f16 (unknown rmsnorm variant)")
+        _chk(x.dim() == 2, f"x 必须是 2 维 (M, H)，实际 {x.dim()} 维 (x must be 2-D)")
+        _chk(w.dim() == 1, f"w 必须是 1 维 (H,)，实际 {w.dim()} 维 (w must be 1-D)")
+        _chk(x.size(0) > 0, f"M 必须 > 0，实际 {x.size(0)} (M must be > 0)")
+        _chk(x.size(1) > 0, f"H 必须 > 0，实际 {x.size(1)} (H must be > 0)")
+        _chk(x.size(1) == w.size(0), f"维度不匹配: H={x.size(1)} vs w={w.size(0)} "
+                                     "(H must equal len(w))")
+        _chk(x.dtype == w.dtype, "x 与 w 必须同 dtype (x and w must have the same dtype)")
+        _chk(x.dtype == torch.float16, f"only float16 rows are supported, got {x.dtype}")
+        _chk(x.is_contiguous(), "x 必须是连续内存 (x must be contiguous)")
+        _chk(w.is_contiguous(), "w 必须是连续内存 (w must be contiguous)")
+        _chk(x.is_cuda, "x 必须是 CUDA 张量 (x must be a CUDA tensor)")
+        _chk(w.is_cuda, "w 必须是 CUDA 张量 (w must be a CUDA tensor)")
+        _chk(x.device == w.device, "w 必须与 x 在同一 CUDA 设备上 (w must be on the device of x)")
+        _chk(eps >= 0.0 and eps == eps and eps != float("inf"),
+             f"eps 必须是有限且 >= 0，实际 {eps} (eps must be finite and >= 0)")
+        _chk(x.size(1) % 8 == 0, f"H must be a multiple of 8, got {x.size(1)}")
+
+    def _launch(self, x, w, out, eps: float, flags: int) -> None:
+        dev = x.device
+        with torch.cuda.device(dev):
+            rc = self._lib.cl_rmsnorm_f16(x.data_ptr(), w.data_ptr(), float(eps), out.data_ptr(),
+                                          x.size(0), x.size(1), _stream_ptr(dev), flags)
+        if rc != nat.CL_OK:
+            raise RuntimeError(f"rmsnorm launch failed ({rc}): {nat.last_error(self._lib)}")
+
+    def forward(self, variant: str, x, w, eps: float = 1e-5, flags: int = 0) -> torch.Tensor:
+        self._validate(variant, x, w, eps)
+        out = torch.empty_like(x)
+        self._launch(x, w, out, eps, flags)
+        return out
+
+    def forward_into(self, variant: str, x, w, out, eps: float = 1e-5, flags: int = 0) -> None:
+        self._validate(variant, x, w, eps)
+        _chk(out.dim() == 2, f"out 必须是 2 维 (M, H)，实际 {out.dim()} 维 (out must be 2-D)")
+        _chk(out.shape == x.shape, "out 形状必须与 x 一致 (out must have the shape of x)")
+        _chk(out.dtype == x.dtype, "out 必须与 x 同 dtype (out must have the dtype of x)")
+        _chk(out.is_contiguous(), "out 必须是连续内存 (out must be contiguous)")
+        _chk(out.is_cuda, "out 必须是 CUDA 张量 (out must be a CUDA tensor)")
+        _chk(out.device == x.device, "out 必须与 x 在同一 CUDA 设备上 (out must be on the "
+                                     "device of x)")
+        self._launch(x, w, out, eps, flags)
+
+
+_EXT_TYPES = {"int4gemv": Int4gemvExt, "qgemv": QgemvExt, "gemv": GemvExt, "rmsnorm": RmsnormExt}
 
 
 def get_ext(op: str):

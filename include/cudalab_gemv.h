@@ -126,6 +126,37 @@ int cl_int4gemv_native_timing(const char* variant, const uint8_t* W_packed, cons
  * required including the terminator. */
 int cl_int4gemv_list_variants(int which, char* buf, size_t buf_len, size_t* needed);
 
+/* ---- RMSNorm and the fused RMSNorm -> INT4 GEMV ----
+ *
+ * RMSNorm of fp16 rows with the arithmetic of the reference's rmsnorm_ref
+ * (cudalab/reference.py:41-45) and its v4 kernel (kernels/rmsnorm/
+ * rmsnorm_v4.cu:84-108): v = mean(x^2) accumulated in fp32, r = 1 / sqrt(v +
+ * eps) (correctly rounded here), y = fp16((x * r) * w).
+ *
+ * cl_rmsnorm_f16 replaces the fp16 path of `forward_into` of the reference's
+ * rmsnorm operator (kernels/rmsnorm/bindings.cpp:43-55, 110): X, Y fp16
+ * [M, H], weight fp16 [H]; H a multiple of 8 and at most 3 * 2^20, pointers
+ * 16-byte aligned, eps finite and >= 0 (bindings.cpp:40).
+ *
+ * cl_int4gemv_rmsnorm has no reference counterpart: Y[m] = W * RMSNorm(X[m],
+ * norm_weight) in one launch per 16 rows (the decoder step "norm, then the
+ * quantised projection").  Each CTA reduces the whole activation row and
+ * normalises the words it stages, so the normalised activations never go to
+ * memory.  W_packed / scale / K as for cl_int4gemv; X fp16 [M, K] and Y fp16
+ * [M, N] contiguous; norm_weight fp16 [K]; X, W_packed and norm_weight
+ * 16-byte aligned.  The result equals cl_rmsnorm_f16 followed by
+ * cl_int4gemv_batched with variant int4gemv_mma_w8c2 (same geometry), bit for
+ * bit.  Variants: int4gemv_rmsnorm (geometry per call) and
+ * int4gemv_rmsnorm_w2 / _w4 / _w8 / _w8c2 / _w16 (fixed geometry; all give
+ * the same bits).  norm_weight is read like W_packed: possibly before the
+ * preceding kernel on the stream has completed (under CL_LAUNCH_PDL), so it
+ * must not be written by that kernel. */
+int cl_rmsnorm_f16(const void* X, const void* weight, float eps, void* Y, int64_t M, int64_t H,
+                   void* stream, uint32_t flags);
+int cl_int4gemv_rmsnorm(const char* variant, const uint8_t* W_packed, const void* scale,
+                        const void* X, const void* norm_weight, float eps, void* Y, int64_t M,
+                        int64_t N, int64_t K, void* stream, uint32_t flags);
+
 /* ---- INT8 ---- */
 
 /* Replaces `forward` / `forward_into` of kernels/qgemv/bindings.cpp:66-115
