@@ -29,6 +29,9 @@ sharded = the row-sharded 70B-class MLP shapes (28672x8192 and 8192x28672,
           N x the measured HBM bandwidth, plus an in-run parity check (fused ==
           NCCL bit for bit, shard rows == the single-GPU kernel, sampled rows
           inside the reference's arithmetic bound): `sharded_parity`.
+rmsnorm_fused = RMSNorm -> INT4 GEMV over the same pool (M = 1): the fused
+          launch (chained and with x ready) and the unfused pair (RMSNorm
+          kernel, then the GEMV), with an in-run bit-equality check.
 --gpus N under torchrun: every rank runs its own pool for the headline (weak
 scaling, no data-path collective; only the timing reduction uses NCCL); the
 sharded block exchanges y between the ranks.
@@ -231,6 +234,52 @@ def cpu_baseline_sample():
             "sample": f"{n} full 4096x4096 GEMVs (dequantise to fp32 + fp32 mv), "
                       f"{dt * 1e3:.2f} ms each, ~10 s total",
             "int8_ms_per_gemv": round(dt8 * 1e3, 3)}
+
+
+def rmsnorm_block(pool, ext, ext_norm, capture, replay_us, mode_flags, variant, peak, reps):
+    """us per layer of RMSNorm -> INT4 GEMV over the pool: fused (one launch)
+    and unfused (RMSNorm kernel, then the GEMV), chained and with x ready."""
+    import torch
+    weights, xs = pool.shared["weights"], pool.xs
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2024)
+    gw = (torch.randn(K_COLS, generator=gen, device="cuda") * 0.5 + 1.0).half()
+    xn = torch.empty(POOL, 1, K_COLS, dtype=torch.float16, device="cuda")
+    ys = torch.empty(POOL, N_ROWS, dtype=torch.float16, device="cuda")
+    ys2 = torch.empty_like(ys)
+
+    class _Fused:
+        def launch(self, e, v, i, flags=0):
+            W, sc = weights[i]
+            e.forward_rmsnorm("int4gemv_rmsnorm", W, sc, xs[i], gw, out=ys[i], flags=flags)
+
+    class _Unfused:
+        def launch(self, e, v, i, flags=0):
+            W, sc = weights[i]
+            ext_norm.forward_into("rmsnorm_f16", xs[i].view(1, K_COLS), gw, xn[i], flags=flags & 1)
+            # x of the GEMV is the preceding kernel's output: PDL only
+            e.forward_into(v, W, sc, xn[i].view(K_COLS), ys2[i], flags=flags & 1)
+
+    out = {"workload": f"{N_ROWS}x{K_COLS} M=1, L2-cold pool of {POOL}, eps 1e-5"}
+    fused, unfused = _Fused(), _Unfused()
+    for m in ("chained", "independent"):
+        gf = capture(fused, ext, variant, mode_flags[m])
+        out[f"fused_{m}_us"] = round(replay_us(gf, reps), 4)
+        del gf
+    gu = capture(unfused, ext, variant, mode_flags["chained"])
+    out["unfused_chained_us"] = round(replay_us(gu, reps), 4)
+    del gu
+    torch.cuda.synchronize()
+    out["parity_fused_equals_unfused"] = bool(torch.equal(ys.view(torch.int16),
+                                                          ys2.view(torch.int16)))
+    nbytes = algo_bytes() + 2 * K_COLS  # + the norm weight
+    t = out["fused_independent_us"]
+    out["roofline"] = {"bound": "hbm", "achieved": round(nbytes / (t * 1e-6) / 1e9, 1),
+                       "peak": peak, "unit": "GB/s",
+                       "frac": round(nbytes / (t * 1e-6) / 1e9 / peak, 4),
+                       "algorithmic_bytes_per_launch": nbytes}
+    out["fused_speedup_chained"] = round(out["unfused_chained_us"] / out["fused_chained_us"], 3)
+    return out
 
 
 def main():
@@ -438,6 +487,12 @@ def main():
     gd = capture(poold, extd, "gemv_mma", flags)
     usd = replay_us(gd, args.context_reps)
     del gd, poold
+    # Fused RMSNorm -> INT4 GEMV on the same L2-cold pool (M = 1), against
+    # the unfused pair (RMSNorm kernel, then the GEMV of its output), in the
+    # chained mode of a decoder step (x written by the preceding kernel) and
+    # with x ready; bit-equality of the two paths checked in-run
+    rms = rmsnorm_block(pool, ext, build("rmsnorm"), capture, replay_us, mode_flags,
+                        args.variant, peak, args.context_reps)
     # The reference's own "streaming" pool (x and y rotate, one weight set, so
     # on B200 the 8.7 MB of weights stay in L2): context only, the headline
     # rotates 64 weight sets through HBM
@@ -507,6 +562,7 @@ def main():
                                        / 1e9, 1),
                           "frac_of_peak": round(algorithmic_bytes_gemv(N_ROWS, K_COLS, 2)
                                                 / (usd * 1e-6) / 1e9 / peak, 4)},
+            "rmsnorm_fused": rms,
             "gpu_launches": launches,
             "device_status": status,
             # the timed region of a short run is shorter than the sampling

@@ -97,6 +97,33 @@ def test_noalloc_entry_rejects_before_device_work(lib):
     assert "16-byte" in nat.last_error(lib)
 
 
+def test_rmsnorm_entries_reject_before_device_work(lib):
+    # every host-side contract check of the RMSNorm and fused entry points
+    # returns before the first CUDA call, so these run without a GPU
+    fake = 1 << 20
+    r = lib.cl_rmsnorm_f16
+    assert r(fake, fake, 1e-5, fake, 0, 64, None, 0) == nat.CL_ERR_INVALID_ARGUMENT
+    assert r(fake, fake, 1e-5, fake, 2, 60, None, 0) == nat.CL_ERR_INVALID_ARGUMENT
+    assert "multiple of 8" in nat.last_error(lib)
+    assert r(fake, fake, 1e-5, fake, 2, 4 << 20, None, 0) == nat.CL_ERR_INVALID_ARGUMENT
+    assert r(fake, fake, -1.0, fake, 2, 64, None, 0) == nat.CL_ERR_INVALID_ARGUMENT
+    assert r(fake, fake, float("inf"), fake, 2, 64, None, 0) == nat.CL_ERR_INVALID_ARGUMENT
+    assert "eps" in nat.last_error(lib)
+    assert r(None, fake, 1e-5, fake, 2, 64, None, 0) == nat.CL_ERR_INVALID_ARGUMENT
+    f = lib.cl_int4gemv_rmsnorm
+    assert f(b"int4gemv_mma", fake, fake, fake, fake, 1e-5, fake, 1, 64, 256, None, 0) == \
+        nat.CL_ERR_UNKNOWN_VARIANT
+    assert f(b"int4gemv_rmsnorm", fake, fake, fake, fake, 1e-5, fake, 0, 64, 256, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert f(b"int4gemv_rmsnorm", fake, fake, fake, fake, 1e-5, fake, 1, 64, 200, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert "128" in nat.last_error(lib)
+    assert f(b"int4gemv_rmsnorm", fake, fake, fake, None, 1e-5, fake, 1, 64, 256, None, 0) == \
+        nat.CL_ERR_INVALID_ARGUMENT
+    assert f(b"int4gemv_rmsnorm", fake, fake, fake, fake, float("nan"), fake, 1, 64, 256, None,
+             0) == nat.CL_ERR_INVALID_ARGUMENT
+
+
 def test_product_has_no_oracle_dependency():
     """The package never imports the checker (oracle/)."""
     pkg = ROOT / "cudalab_b200"
