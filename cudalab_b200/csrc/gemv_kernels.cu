@@ -427,8 +427,12 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
         }
         g.norm_w = static_cast<const __half*>(a.norm_w);
         g.norm_eps = a.norm_eps;
+        // Every launch is a programmatic dependent launch; without the
+        // caller's CL_LAUNCH_PDL the kernel waits for the preceding kernel
+        // before touching global memory (stream order, launch latency hidden)
+        g.wait_first = (flags & 1u) ? 0 : 1;
         return launch(kernel, dim3((unsigned)(g.groups * g.splits)), dim3(32 * kWarps),
-                      (size_t)smem, s, flags, g.splits, static_cast<const uint8_t*>(a.W),
+                      (size_t)smem, s, flags | 1u, g.splits, static_cast<const uint8_t*>(a.W),
                       static_cast<const S*>(a.scale), static_cast<const __half*>(a.x),
                       static_cast<__half*>(a.y), g, po);
     };
@@ -672,7 +676,8 @@ cudaError_t launch_tc_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, co
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const TcGeom g = make_tc_geom(a, sm_count(dev));
+    TcGeom g = make_tc_geom(a, sm_count(dev));
+    g.wait_first = (flags & 1u) ? 0 : 1;  // launched with PDL either way (see launch_mma_impl)
     CUtensorMap map;
     if ((e = int4_weight_map(a.W, a.N, a.K, map)) != cudaSuccess) return e;
     auto kernel = gemv_tc_int4_kernel<kPeer>;
@@ -680,7 +685,7 @@ cudaError_t launch_tc_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, co
     if ((e = ensure_smem_attr(kernel, dev, smem)) != cudaSuccess) return e;
     const int64_t tiles = (a.N + kTcRows - 1) / kTcRows;
     return launch(kernel, dim3((unsigned)(tiles * g.splits)), dim3(kTcThreads), (size_t)smem, s,
-                  flags, g.splits, map, static_cast<const __half*>(a.scale),
+                  flags | 1u, g.splits, map, static_cast<const __half*>(a.scale),
                   static_cast<const __half*>(a.x), static_cast<__half*>(a.y), g, po);
 }
 

@@ -83,6 +83,7 @@ struct MmaGeom {
     const __half* norm_w;         // RMSNorm weight [K] (fused-prologue kernels)
     float norm_eps;
     int32_t norm_units;           // RMSNorm unit sums per row of one split (0: no RMSNorm)
+    int32_t wait_first;           // wait for the preceding kernel before any global access
 };
 
 constexpr int kZeroRegion = 256;  // bytes of zeros ahead of the staged activations
@@ -794,6 +795,10 @@ gemv_mma_kernel(const uint8_t* __restrict__ W, const typename Fmt::Scale* __rest
     const uint64_t pol = policy_evict_first();
 
     pdl_allow_dependents();
+    // Without the caller's CL_LAUNCH_PDL the launch still overlaps the
+    // preceding kernel's tail, but touches no global memory before that
+    // kernel has completed: the result is that of stream order.
+    if (g.wait_first) pdl_wait_prior_grids();
     // Segments of this warp: w, w + kWarps, ... in (tile, seg) order, each
     // walked chunk by chunk.  Weights and scales never depend on the preceding
     // kernel: the first two items are requested before waiting on it.

@@ -87,6 +87,7 @@ struct TcGeom {
     int32_t splits;              // K splits (cluster size when > 1)
     int32_t gsplit;              // groups per split (the last split may have fewer)
     long long wait_cycles;       // bound of every mbarrier wait (SM cycles)
+    int32_t wait_first;          // wait for the preceding kernel before any global access
 };
 
 // Shared memory: [weight stages | activation tiles | split row sums | barriers]
@@ -258,6 +259,9 @@ gemv_tc_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __half* __re
     const bool mma_thread = warp == kTcRowWarps && lane == 0;
 
     pdl_allow_dependents();
+    // Without the caller's CL_LAUNCH_PDL: launched early all the same, but no
+    // global access before the preceding kernel has completed (stream order).
+    if (g.wait_first) pdl_wait_prior_grids();
     if (tid == 0) {
         for (int i = 0; i < kTcStages; ++i) mbar_init(b_wfull + 8 * i, 1);
         for (int j = 0; j < kTcABufs; ++j) {
