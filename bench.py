@@ -548,7 +548,8 @@ def main():
                     "h2d_bytes_per_step": POOL * K_COLS * 2,
                     "d2h_bytes_per_step": POOL * N_ROWS * 2,
                     "us_per_gemv": round(e2e_s * 1e6 / (POOL * args.e2e_steps), 2),
-                    "note": "public API (forward_into over the C ABI, one call per GEMV, same "
+                    "note": "public API (forward_into: torch binding checks, then the C ABI; "
+                            "one call per GEMV, same "
                             "flags as the headline): per step the 64 x vectors H2D from pinned "
                             "memory in one copy and the 64 y vectors D2H in one copy, host "
                             "synchronised; wall clock; weights resident"},

@@ -103,9 +103,65 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     return LIB_PATH
 
 
+# ---- the torch binding of the success path (csrc/torch_fast.cpp) ----
+BINDING_SRC = CSRC / "torch_fast.cpp"
+BINDING_NAME = "_cl_torch"
+BINDING_STAMP = LIB_DIR / f"{BINDING_NAME}.stamp.json"
+
+
+def binding_path() -> Path:
+    import sysconfig
+    return LIB_DIR / (BINDING_NAME + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def _binding_cmd(out: Path) -> list[str]:
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    inc = ce.include_paths("cuda") + [sysconfig.get_paths()["include"]]
+    torch_lib = ce.library_paths("cuda")[0]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    return (["g++", "-O2", "-std=c++17", "-fPIC", "-shared", str(BINDING_SRC), "-o", str(out),
+             f"-DTORCH_EXTENSION_NAME={BINDING_NAME}", "-DTORCH_API_INCLUDE_EXTENSION_H",
+             f"-D_GLIBCXX_USE_CXX11_ABI={abi}"]
+            + [f"-I{p}" for p in inc]
+            + [f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+               f"-L{LIB_DIR}", "-lcudalab_gemv", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"])
+
+
+def _binding_fingerprint() -> str:
+    import torch
+    h = hashlib.sha256()
+    for f in (BINDING_SRC, HEADER):
+        h.update(f.read_bytes())
+    h.update(torch.__version__.encode())
+    return h.hexdigest()[:16]
+
+
+def build_binding(force: bool = False) -> Path:
+    """Compile the torch binding (g++, torch headers) next to the library."""
+    out = binding_path()
+    fp = _binding_fingerprint()
+    if not force and out.exists() and BINDING_STAMP.exists():
+        try:
+            if json.loads(BINDING_STAMP.read_text()).get("hash") == fp:
+                return out
+        except (OSError, ValueError):
+            pass
+    tmp = out.with_name(out.name + ".tmp")
+    proc = subprocess.run(_binding_cmd(tmp), capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError("g++ failed on torch_fast.cpp:\n" + proc.stdout + proc.stderr)
+    os.replace(tmp, out)
+    BINDING_STAMP.write_text(json.dumps({"hash": fp}, indent=2))
+    return out
+
+
 def build(op: str = "int4gemv", force: bool = False, verbose: bool = False):
-    """Return the extension object of operator `op` ("int4gemv" | "qgemv" | "gemv")."""
+    """Return the extension object of operator `op` ("int4gemv" | "qgemv" | "gemv" |
+    "rmsnorm")."""
     build_library(force=force, verbose=verbose)
+    build_binding(force=force)
     from .ext import get_ext
     return get_ext(op)
 

@@ -79,12 +79,34 @@ def _same_device(idx: int, *ts) -> bool:
     return True
 
 
+_BINDING = []  # [module or None], loaded once
+
+
+def _binding():
+    """The torch binding of the success path (csrc/torch_fast.cpp), built in
+    the library folder by build.build_binding; None when it is absent, in
+    which case every call takes the ctypes path (the same C ABI and kernels)."""
+    if not _BINDING:
+        mod = None
+        from .build import binding_path
+        p = binding_path()
+        if p.exists():
+            import importlib.util
+            spec = importlib.util.spec_from_file_location("cudalab_b200._cl_torch", p)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+        _BINDING.append(mod)
+    return _BINDING[0]
+
+
 class _ExtBase:
     kind = ""          # "int4gemv" | "qgemv"
     w_name = ""        # "W_packed" | "W_q"
+    _kind_code = -1    # operator code of the torch binding
 
     def __init__(self) -> None:
         self._lib = nat.load()
+        self._tb = _binding()
         self._cache = {}
         # every registered name (normal and quarantined) -> its bytes for the C call
         self._encoded = {v: v.encode() for v in self.all_variants()}
@@ -165,7 +187,13 @@ class _ExtBase:
                                 and out.is_contiguous() and _same_device(W.get_device(), out)))
 
     # ---- public API (names and keyword names of the reference module) ----
+    # The torch binding takes the common call whole (checks in C++, then the C
+    # ABI); whenever it declines, the ordered checks below run and raise.
     def forward(self, variant: str, W, scale, x, flags: int = 0) -> torch.Tensor:
+        if self._tb is not None:
+            out = self._tb.forward(self._kind_code, variant, W, scale, x, flags)
+            if out is not None:
+                return out
         if not self._fast_ok(variant, W, scale, x, None):
             self._check_variant(variant)
             self._validate_inputs(W, scale, x)
@@ -174,6 +202,9 @@ class _ExtBase:
         return out
 
     def forward_into(self, variant: str, W, scale, x, out, flags: int = 0) -> None:
+        if self._tb is not None and \
+                self._tb.forward_into(self._kind_code, variant, W, scale, x, out, flags) == 0:
+            return
         if not self._fast_ok(variant, W, scale, x, out):
             self._check_variant(variant)
             self._validate_inputs(W, scale, x)
@@ -248,6 +279,7 @@ class Int4gemvExt(_ExtBase):
     """W4A16: W_packed uint8 [N, K/2], scale fp16 [N, K/128], x fp16 [K]."""
     kind = "int4gemv"
     w_name = "W_packed"
+    _kind_code = 0
 
     def __init__(self) -> None:
         super().__init__()
@@ -348,6 +380,7 @@ class QgemvExt(_ExtBase):
     """INT8: W_q int8 [N, K], scale fp32 [N], x fp16 [K]."""
     kind = "qgemv"
     w_name = "W_q"
+    _kind_code = 1
 
     def __init__(self) -> None:
         super().__init__()
