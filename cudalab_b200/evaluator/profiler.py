@@ -82,6 +82,8 @@ def driver_main(argv=None) -> int:
     ap.add_argument("--pool", type=int, default=4)
     ap.add_argument("--launches", type=int, default=6)
     ap.add_argument("--pdl", type=int, default=0)
+    ap.add_argument("--rmsnorm", action="store_true",
+                    help="fused RMSNorm -> INT4 GEMV (variant int4gemv_rmsnorm*), M rows")
     a = ap.parse_args(argv)
     sys.path.insert(0, str(ROOT))
     import torch
@@ -90,7 +92,15 @@ def driver_main(argv=None) -> int:
     op = get(a.op)
     ext = build(a.op)
     pool = op.make_bench_pool(a.N, a.K, mode="l2cold", pool_size=a.pool, weight_dist=0.02)
-    if a.M == 1:
+    if a.rmsnorm:
+        X = torch.randn(a.M, a.K, device="cuda").half()
+        gw = (torch.randn(a.K, device="cuda") * 0.5 + 1.0).half()
+        Y = torch.empty(a.M, a.N, device="cuda", dtype=torch.float16)
+        weights = pool.shared["weights"]
+        for i in range(a.launches):
+            W, s = weights[i % len(weights)]
+            ext.forward_rmsnorm(a.variant, W, s, X, gw, out=Y, flags=a.pdl)
+    elif a.M == 1:
         for i in range(a.launches):
             pool.launch(ext, a.variant, i, flags=a.pdl)
     else:
