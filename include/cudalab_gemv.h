@@ -273,10 +273,9 @@ int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void*
  * with CL_ERR_INVALID_ARGUMENT); y receives W x, the same bits as
  * cl_int4gemv_ex / cl_int4gemv_batched with the same variant family.  The
  * scratch is one flag block whatever N, K and M are.  The first call on a
- * device looks up the array's device address (make it before any stream
- * capture); so does the first call after the device's context changed (e.g.
- * after cudaDeviceReset, which loads the library's device code again at a new
- * address), which should likewise come before any capture.  Every call clears
+ * device looks up the array's device address; so does the first call after
+ * the device's context changed (e.g. after cudaDeviceReset, which loads the
+ * library's device code again at a new address).  Every call clears
  * the block on `stream` before its kernel.  All calls share the one block:
  * calls that overlap on the GPU (other streams, other threads) race and must
  * be serialised by the caller. */
