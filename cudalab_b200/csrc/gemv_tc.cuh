@@ -356,13 +356,15 @@ gemv_tc_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __half* __re
                                      g.wait_cycles);
         };
         uint4 xv = load_x(0);
-        float s_lag = 0.f;  // scale of group gi - kTcDBufs, loaded one iteration ahead
+        // scale of group gi - kTcDBufs, loaded one iteration ahead and kept as
+        // fp16 until its use, so the load's latency is not paid where it is issued
+        __half s_lag = __float2half(0.f);
         int released = 0;   // groups released to the MMA thread
         for (int gi = 0; gi < G; ++gi) {
             const int j = gi % kTcABufs;
             const int lagged = gi - kTcDBufs;
             const uint4 xv_next = gi + 1 < G ? load_x(gi + 1) : make_uint4(0u, 0u, 0u, 0u);
-            const float s_lag_next = lagged + 1 >= 0 ? __half2float(srow_p[lagged + 1]) : 0.f;
+            const __half s_lag_next = lagged + 1 >= 0 ? srow_p[lagged + 1] : __float2half(0.f);
             if (gi >= 1) {
                 release(gi - 1);
                 released = gi;
@@ -431,8 +433,9 @@ gemv_tc_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __half* __re
             // released to the MMA thread only after this read
             if (lagged >= 0) {
                 tc_ld8_wait(dr);
+                const float sl = __half2float(s_lag);
 #pragma unroll
-                for (int m = 0; m < 8; ++m) yacc[m] = fmaf(s_lag, __uint_as_float(dr[m]), yacc[m]);
+                for (int m = 0; m < 8; ++m) yacc[m] = fmaf(sl, __uint_as_float(dr[m]), yacc[m]);
             }
             s_lag = s_lag_next;
         }
