@@ -222,18 +222,28 @@ struct PeerOut {
     int rank, world;
 };
 
+// Ticket of a CTA: acquire-release at GPU scope (every CTA of the grid is on
+// this GPU).
+__device__ __forceinline__ unsigned ticket_acq_rel_gpu(unsigned* p) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p) : "memory");
+    return prev;
+}
+
 // Called by thread 0 of every CTA after a CTA barrier that follows the CTA's
-// peer stores: the system-scope fence before the ticket publishes the whole
-// CTA's stores (cumulativity through the barrier); the last CTA's fence and
-// the strong stores after it (a release pattern: one fence for all peers, not
-// one per peer as st.release would imply) publish every CTA's stores (through
-// the ticket atomics).  Loops run over the compile-time peer slots so that
-// `po` stays in the parameter space (no local copy).
+// peer stores.  The ticket is a release at GPU scope (through the barrier it
+// covers the whole CTA's stores) and, for the last CTA, an acquire of every
+// other CTA's release; the last CTA's system-scope fence and the strong flag
+// stores after it (a release pattern: one fence for all peers, not one per
+// peer as st.release would imply) then order all of them before each peer's
+// acquire of its flag: causality order is transitive across the two scopes,
+// so one system fence per step replaces one per CTA.  Loops run over the
+// compile-time peer slots so that `po` stays in the parameter space (no
+// local copy).
 __device__ __forceinline__ void peer_arrive_and_wait(const PeerOut& po, unsigned epoch,
                                                      long long budget) {
     unsigned* mine = po.flag[po.rank];
-    __threadfence_system();
-    const unsigned prev = atomicAdd(mine + kTicket, 1u);
+    const unsigned prev = ticket_acq_rel_gpu(mine + kTicket);
     if (prev != gridDim.x - 1) return;
     atomicExch(mine + kTicket, 0u);
     __threadfence_system();
