@@ -489,18 +489,39 @@ cudaError_t launch_tc(const GemvArgs& a, cudaStream_t s, unsigned flags);
 cudaError_t launch_tc_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream_t s,
                               unsigned flags);
 
-// INT4 with 9..16 activation rows on few row tiles (fewer than half an SM
+// K split of the tensor-core kernel (gemv_tc.cuh) for `tiles` 128-row tiles
+// and `groups` scale groups: doubled while the grid stays within one wave of
+// resident CTAs (two per SM) and every split keeps at least two weight stages.
+int64_t tc_split_count(int64_t tiles, int64_t groups, int num_sms) {
+    int64_t S = 1;
+    while (S < kTcMaxSplits && tiles * 2 * S <= 2 * (int64_t)num_sms && groups / (2 * S) >= 4)
+        S *= 2;
+    return S;
+}
+
+// INT4 with 15 or 16 activation rows on few row tiles (fewer than half an SM
 // each, so K is split across a cluster) runs the 5th-generation tensor-core
-// kernel (gemv_tc.cuh), measured faster there than the register-fed kernel
-// (4096 x 4096: 10.2 vs 12.0 us; 8192 x 28672: 67.4 vs 76.1 us); the
-// register-fed kernel keeps the rest (28672 x 8192: 56 vs 73 us).  The choice
+// kernel, whose cost does not grow with the number of rows, when its grid
+// has at least one CTA per SM and each split at least 8 scale groups (any
+// split at 16 rows); the register-fed kernel, whose cost grows with the rows,
+// keeps everything else.  Measured on two B200 boxes with L2-cold pools (the
+// tensor-core kernel is latency-bound and the more clock-sensitive of the two,
+// so the rule keeps the cases it won on both), us tcgen05 vs register-fed at
+// 16 rows: 8192x28672 55.2 / 70.9 vs 72.5 / 75.2; 7168x8192 21.8 / 26.0 vs
+// 28.3 / 28.6; 4096x4096 10.6 / 11.7 vs 11.8 / 12.1; 2048x28672 (128 CTAs)
+// 29.8 / 37.6 vs 29.3 / 31.9; at 12 rows the two boxes disagree.  The choice
 // depends on the shape and the SM count only.
 template <class Fmt>
 bool prefer_tc(const GemvArgs& a) {
-    if (!Fmt::kGroupScale || a.M <= 8) return false;
+    if (!Fmt::kGroupScale || a.M < 15) return false;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
-    return 2 * ((a.N + 127) / 128) < (int64_t)sm_count(dev);
+    const int sms = sm_count(dev);
+    const int64_t tiles = (a.N + 127) / 128, groups = a.K / 128;
+    if (2 * tiles >= (int64_t)sms) return false;
+    const int64_t S = tc_split_count(tiles, groups, sms);
+    if (tiles * S < (int64_t)sms) return false;
+    return a.M == 16 || (groups + S - 1) / S >= 8;
 }
 
 template <class Fmt>
@@ -657,8 +678,7 @@ TcGeom make_tc_geom(const GemvArgs& a, int num_sms) {
     g.groups = (int32_t)(a.K / kTcGroupK);
     g.wait_cycles = g_wait_budget.load(std::memory_order_relaxed);
     const int64_t tiles = (a.N + kTcRows - 1) / kTcRows;
-    int64_t S = 1;
-    while (S < kTcMaxSplits && tiles * S < 2 * (int64_t)num_sms && g.groups / (2 * S) >= 4) S *= 2;
+    const int64_t S = tc_split_count(tiles, g.groups, num_sms);
     const int64_t gs = (g.groups + S - 1) / S;
     g.gsplit = (int32_t)gs;
     g.splits = (int32_t)((g.groups + gs - 1) / gs);  // no empty split
