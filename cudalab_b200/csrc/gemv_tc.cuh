@@ -526,20 +526,45 @@ gemv_tc_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __half* __re
             for (int m = 0; m < 8; ++m) rsum[my_row * kTcN + 8 * half + m] = yacc[m];
         }
         cluster_sync_all();
-        // split s finishes rows [s * span, (s + 1) * span) of the tile
+        // split s finishes activation rows [s * mspan, (s + 1) * mspan) of the
+        // tile's rows (sums in split order), eight consecutive tile rows per
+        // thread: one 16-byte store per destination where it is aligned, so
+        // every rank's buffer receives whole 256-byte runs of a row of Y
         const int64_t left = g.N - row0;
         const int nrows = left < kTcRows ? (int)left : kTcRows;
-        const int span = (nrows + g.splits - 1) / g.splits;
-        const int lo = min(nrows, split * span), hi = min(nrows, lo + span);
+        const int mspan = (g.M + g.splits - 1) / g.splits;
+        const int mlo = min(g.M, split * mspan), mhi = min(g.M, mlo + mspan);
+        const int nvec = (nrows + 7) / 8;
         bool any_fail = false;
         const uint32_t fail_addr = smem_u32(const_cast<int*>(s_fail));
         for (int sp = 0; sp < g.splits; ++sp) any_fail |= ld_cluster_u32(fail_addr, sp) != 0u;
         if (!any_fail) {
-            for (int idx = tid; idx < (hi - lo) * g.M; idx += kTcThreads) {
-                const int rr = lo + idx / g.M, m = idx % g.M;
-                float s = 0.f;
-                for (int sp = 0; sp < g.splits; ++sp) s += ld_cluster_f32(rsum + rr * kTcN + m, sp);
-                store(row0 + rr, m, s);
+            for (int idx = tid; idx < (mhi - mlo) * nvec; idx += kTcThreads) {
+                const int m = mlo + idx / nvec, r8 = 8 * (idx % nvec);
+                const int cnt = min(8, nrows - r8);
+                uint32_t h2[4] = {0u, 0u, 0u, 0u};
+                __half* hv = reinterpret_cast<__half*>(h2);
+                for (int i = 0; i < cnt; ++i) {
+                    float v = 0.f;
+                    for (int sp = 0; sp < g.splits; ++sp)
+                        v += ld_cluster_f32(rsum + (r8 + i) * kTcN + m, sp);
+                    hv[i] = __float2half_rn(v);
+                }
+                auto put = [&](__half* dst) {
+                    if (cnt == 8 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+                        *reinterpret_cast<uint4*>(dst) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+                    } else {
+                        for (int i = 0; i < cnt; ++i) dst[i] = hv[i];
+                    }
+                };
+                if constexpr (kPeer) {
+                    const int64_t off = m * g.y_stride + po.row0 + row0 + r8;
+#pragma unroll
+                    for (int p = 0; p < kMaxPeers; ++p)
+                        if (p < po.world) put(((epoch & 1) ? po.y[1][p] : po.y[0][p]) + off);
+                } else {
+                    put(y + m * g.y_stride + row0 + r8);
+                }
             }
         }
         // no CTA leaves while the others may still read its row sums
