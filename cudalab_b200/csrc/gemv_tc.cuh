@@ -523,7 +523,9 @@ gemv_tc_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __half* __re
     } else {
         if (warp < kTcRowWarps) {
 #pragma unroll
-            for (int m = 0; m < 8; ++m) rsum[my_row * kTcN + 8 * half + m] = yacc[m];
+            // [activation row][tile row]: a warp writes, and a split later
+            // reads, contiguous runs of one activation row
+            for (int m = 0; m < 8; ++m) rsum[(8 * half + m) * kTcRows + my_row] = yacc[m];
         }
         cluster_sync_all();
         // split s finishes activation rows [s * mspan, (s + 1) * mspan) of the
@@ -539,24 +541,31 @@ gemv_tc_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __half* __re
         const uint32_t fail_addr = smem_u32(const_cast<int*>(s_fail));
         for (int sp = 0; sp < g.splits; ++sp) any_fail |= ld_cluster_u32(fail_addr, sp) != 0u;
         if (!any_fail) {
+            // every thread sums (row, activation row) elements over the
+            // splits into a staged copy in the weight-stage area (idle now),
+            // then eight rows at a time go out
+            __half* staged = reinterpret_cast<__half*>(smem);
+            for (int idx = tid; idx < (mhi - mlo) * nrows; idx += kTcThreads) {
+                const int mm = idx / nrows, rr = idx - mm * nrows;
+                float v = 0.f;
+                for (int sp = 0; sp < g.splits; ++sp)
+                    v += ld_cluster_f32(rsum + (mlo + mm) * kTcRows + rr, sp);
+                staged[mm * kTcRows + rr] = __float2half_rn(v);
+            }
+            __syncthreads();
             for (int idx = tid; idx < (mhi - mlo) * nvec; idx += kTcThreads) {
-                const int m = mlo + idx / nvec, r8 = 8 * (idx % nvec);
+                const int mm = idx / nvec, r8 = 8 * (idx - mm * nvec);
                 const int cnt = min(8, nrows - r8);
-                uint32_t h2[4] = {0u, 0u, 0u, 0u};
-                __half* hv = reinterpret_cast<__half*>(h2);
-                for (int i = 0; i < cnt; ++i) {
-                    float v = 0.f;
-                    for (int sp = 0; sp < g.splits; ++sp)
-                        v += ld_cluster_f32(rsum + (r8 + i) * kTcN + m, sp);
-                    hv[i] = __float2half_rn(v);
-                }
+                const __half* src = staged + mm * kTcRows + r8;
+                const uint4 v8 = *reinterpret_cast<const uint4*>(src);
                 auto put = [&](__half* dst) {
                     if (cnt == 8 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-                        *reinterpret_cast<uint4*>(dst) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+                        *reinterpret_cast<uint4*>(dst) = v8;
                     } else {
-                        for (int i = 0; i < cnt; ++i) dst[i] = hv[i];
+                        for (int i = 0; i < cnt; ++i) dst[i] = src[i];
                     }
                 };
+                const int m = mlo + mm;
                 if constexpr (kPeer) {
                     const int64_t off = m * g.y_stride + po.row0 + row0 + r8;
 #pragma unroll
