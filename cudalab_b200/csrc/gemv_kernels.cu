@@ -266,13 +266,14 @@ cudaError_t per_row(const GemvArgs& a, cudaStream_t s, unsigned flags) {
 // Geometry of the tensor-core kernels (see gemv_mma.cuh).
 //   K is split (cluster of up to 8 CTAs) while the row tiles alone cannot
 //   give every SM a CTA or the staged activations of a split exceed the
-//   budget; the row groups then target SMs x ctas_per_sm CTAs (1 for 8-warp
-//   CTAs, 2 for a shorter per-launch latency), capped by max_groups (clusters
+//   budget; the row groups then target SMs x ctas_per_sm / sms_per_cta CTAs
+//   (1 for 8-warp CTAs, 2 for a shorter per-launch latency, one per two SMs
+//   for independent INT4 GEMVs), capped by max_groups (clusters
 //   that can be resident at once).  Returns false when no split fits in
 //   shared memory.  `norm`: room for the fused RMSNorm's unit sums (the split
 //   and every other choice stay those of the plain launch).
 bool make_mma_geom(int64_t N, int64_t K, int64_t M, int kind, int num_sms, int ctas_per_sm,
-                   int64_t max_groups, MmaGeom& g, bool norm = false) {
+                   int64_t max_groups, MmaGeom& g, bool norm = false, int sms_per_cta = 1) {
     g = MmaGeom{};
     g.wait_cycles = g_wait_budget.load(std::memory_order_relaxed);
     g.N = N;
@@ -286,7 +287,7 @@ bool make_mma_geom(int64_t N, int64_t K, int64_t M, int kind, int num_sms, int c
                                             : MmaF16::kBlockWords;
     const int pad = M > 1 ? 4 : 0;  // 64 B between activation rows: no bank conflicts
     const int64_t tiles = (N + 15) / 16;
-    const int64_t target = (int64_t)num_sms * ctas_per_sm;
+    const int64_t target = std::max<int64_t>(1, (int64_t)num_sms * ctas_per_sm / sms_per_cta);
     // Budgets keep two CTAs per SM for M <= 8 (one 16-warp CTA for M > 8).
     const int64_t xs_budget = (M == 1 ? 96 : M <= 8 ? 80 : 144) * 1024;
     auto xs_bytes = [&](int64_t kc_split) {
@@ -361,7 +362,8 @@ cudaError_t max_active_clusters(K kernel, const cudaLaunchConfig_t& cfg, int dev
 // rank's buffers (`po`); the sharded entry points check the contract first.
 // kNorm: fused RMSNorm of the activation rows (a.norm_w, a.norm_eps); no
 // scalar fallback (an unmet contract is an error).
-template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer, bool kNorm = false>
+template <class Fmt, int kWarps, int kCtasPerSm, bool kPeer, bool kNorm = false,
+          int kSmsPerCta = 1>
 cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, const PeerOut& po) {
     constexpr bool kInt4 = Fmt::kGroupScale;
     const bool ok = aligned16(a.W) && aligned16(a.x) && (a.x_stride % 8) == 0 &&
@@ -372,7 +374,8 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
     if (e != cudaSuccess) return e;
     MmaGeom g;
     const bool geom =
-        ok && make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, 0, g, kNorm);
+        ok && make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, 0, g, kNorm,
+                            kSmsPerCta);
     if (!geom) {
         if constexpr (kPeer || kNorm)
             return ok ? cudaErrorInvalidConfiguration : cudaErrorMisalignedAddress;
@@ -415,7 +418,7 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
                 const int64_t x_stride = g.x_stride, y_stride = g.y_stride;
                 const int early = g.early_x, free_y = g.free_y;
                 if (!make_mma_geom(a.N, a.K, a.M, Fmt::kKind, sm_count(dev), kCtasPerSm, clusters,
-                                   g, kNorm))
+                                   g, kNorm, kSmsPerCta))
                     return cudaErrorInvalidConfiguration;
                 g.x_stride = x_stride;
                 g.y_stride = y_stride;
@@ -448,9 +451,10 @@ cudaError_t launch_mma_impl(const GemvArgs& a, cudaStream_t s, unsigned flags, c
                     : go(gemv_mma_kernel<Fmt, kWarps, 2, false, kPeer, kNorm>);
 }
 
-template <class Fmt, int kWarps, int kCtasPerSm>
+template <class Fmt, int kWarps, int kCtasPerSm, int kSmsPerCta = 1>
 cudaError_t launch_mma(const GemvArgs& a, cudaStream_t s, unsigned flags) {
-    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, false>(a, s, flags, PeerOut{});
+    return launch_mma_impl<Fmt, kWarps, kCtasPerSm, false, false, kSmsPerCta>(a, s, flags,
+                                                                           PeerOut{});
 }
 
 template <int kWarps, int kCtasPerSm>
@@ -476,10 +480,16 @@ cudaError_t launch_mma_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream
 }
 
 // Geometry chosen per call (measured on B200 with L2-cold pools):
-//  * independent GEMVs (CL_LAUNCH_PDL | CL_LAUNCH_INPUTS_READY): one CTA per
-//    SM per GEMV with 2 warps (K <= 4096: up to eight GEMVs overlap on an
-//    SM), 4 warps (K <= 16384) or 8 warps (the staged activations then limit
-//    co-residency);
+//  * independent GEMVs (CL_LAUNCH_PDL | CL_LAUNCH_INPUTS_READY): INT4 with
+//    K <= 16384 takes 4-warp CTAs, one per two SMs per GEMV: the same warps
+//    per GEMV as 2-warp CTAs on every SM, but each CTA stages x for twice the
+//    rows, so the per-CTA staging and set-up cost is paid half as often
+//    (us per GEMV against the 2-warp / 4-warp full grids, flags 7: 4096^2
+//    1.888 vs 1.966 and 1.94 vs 2.03 on two boxes; 4096x1024 0.994 vs 1.039;
+//    1024x4096 1.158 vs 1.221; 4096x11008 5.45 vs 5.64; 11008x4096 within
+//    3 % either way); otherwise one CTA per SM per GEMV with 2 warps
+//    (K <= 4096: up to eight GEMVs overlap on an SM), 4 warps (K <= 16384)
+//    or 8 warps (the staged activations then limit co-residency);
 //  * chained or plain launches: 8-warp CTAs, two per SM per GEMV (shorter
 //    per-GEMV latency), one per SM for K <= 2048;
 //  * several activation rows: one CTA per SM per launch; 4 warps (2..8 rows)
@@ -535,6 +545,7 @@ cudaError_t launch_mma_auto(const GemvArgs& a, cudaStream_t s, unsigned flags) {
         return small ? launch_mma<Fmt, 4, 1>(a, s, flags) : launch_mma<Fmt, 8, 1>(a, s, flags);
     }
     if ((flags & 3u) == 3u) {
+        if (Fmt::kGroupScale && a.K <= 16384) return launch_mma<Fmt, 4, 1, 2>(a, s, flags);
         if (a.K <= 4096) return launch_mma<Fmt, 2, 1>(a, s, flags);
         return a.K <= 16384 ? launch_mma<Fmt, 4, 1>(a, s, flags)
                             : launch_mma<Fmt, 8, 1>(a, s, flags);
@@ -742,6 +753,7 @@ const VariantDesc kInt4Variants[] = {
     {"int4gemv_mma_w8", launch_mma<MmaInt4, 8, 1>, false},
     {"int4gemv_mma_w8c2", launch_mma<MmaInt4, 8, 2>, false},
     {"int4gemv_mma_w16", launch_mma<MmaInt4, 16, 1>, false},
+    {"int4gemv_mma_w4h", launch_mma<MmaInt4, 4, 1, 2>, false},
     // The reference's variant names (kernels/int4gemv/*.cu registrars), each
     // bound to the kernel here that fills the same role, so a caller that
     // dispatches by those strings runs unmodified:

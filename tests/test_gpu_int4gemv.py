@@ -67,12 +67,17 @@ FULL = [(4096, 4096), (1024, 4096), (4096, 1024), (11008, 4096), (4096, 11008)]
 
 @pytest.mark.parametrize("shape", FULL, ids=lambda s: f"{s[0]}x{s[1]}")
 @pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_mma_w4", "int4gemv_mma_w8c2",
-                                     "int4gemv_bulk", "int4gemv_ldg"])
+                                     "int4gemv_mma_w4h", "int4gemv_bulk", "int4gemv_ldg"])
 def test_full_size_vs_oracle(ext, variant, shape):
     N, K = shape
     Wp, s, _ = make_w4(N, K, seed=77, scale=0.02)
     x = make_x4(K, seed=78)
     y = ext.forward(variant, Wp, s, x).cpu().numpy()
+    if variant == "int4gemv_mma":
+        # the geometry of independent launches (flags 7) gives the same bits
+        y7 = ext.forward(variant, Wp, s, x, flags=nat.CL_LAUNCH_PDL | nat.CL_LAUNCH_INPUTS_READY
+                         | nat.CL_LAUNCH_OUTPUTS_FREE)
+        assert np.array_equal(y7.cpu().numpy().view(np.uint16), y.view(np.uint16))
     r = orc.check(y, Wp.cpu().numpy(), s.cpu().numpy(), x.cpu().numpy())
     assert r["pass"], r
 
@@ -182,7 +187,7 @@ def _outlier_case(N, K, seed):
 @pytest.mark.parametrize("K", [128, 1024, 4096])
 @pytest.mark.parametrize("variant", ["int4gemv_mma", "int4gemv_mma_w4", "int4gemv_mma_w8",
                                      "int4gemv_mma_w8c2", "int4gemv_mma_w16",
-                                     "int4gemv_baseline"])
+                                     "int4gemv_mma_w4h", "int4gemv_baseline"])
 def test_outlier_groups_vs_oracle(ext, variant, K):
     Wp, s, x = _outlier_case(512, K, seed=K)
     y = ext.forward(variant, Wp, s, x).cpu().numpy()
