@@ -487,7 +487,9 @@ cudaError_t launch_mma_sharded(const GemvArgs& a, const PeerArgs& pa, cudaStream
 //    (us per GEMV against the 2-warp / 4-warp full grids, flags 7: 4096^2
 //    1.888 vs 1.966 and 1.94 vs 2.03 on two boxes; 4096x1024 0.994 vs 1.039;
 //    1024x4096 1.158 vs 1.221; 4096x11008 5.45 vs 5.64; 11008x4096 within
-//    3 % either way); otherwise one CTA per SM per GEMV with 2 warps
+//    3 % either way; paired A/B rounds on one box: 4096^2 flags 7 / 3 +3.0 /
+//    +2.8 %, 11008x4096 +2.5 %, 4096x11008 +3.2 %, 4096x1024 +0.1 %, every
+//    interval but the last above 1); otherwise one CTA per SM per GEMV with 2 warps
 //    (K <= 4096: up to eight GEMVs overlap on an SM), 4 warps (K <= 16384)
 //    or 8 warps (the staged activations then limit co-residency);
 //  * chained or plain launches: 8-warp CTAs, two per SM per GEMV (shorter
