@@ -115,6 +115,17 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The first step of an accumulator chain: d = a b + (+0), the zero taken from
+// one loop-invariant register instead of zeroing d before every chain.
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+    const float z = 0.f;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // Nibbles 0 and 4 of w as an exact half2 (q0, q4) ...
@@ -463,9 +474,6 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
         const uint4* xb = xs + (lb0 >> 2) * 64 + (gq & 3) * 4 + t;
         float acc[kMmaChunkBlocks][4];
 #pragma unroll
-        for (int q = 0; q < kMmaChunkBlocks; ++q)
-            acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
-#pragma unroll
         for (int w = 0; w < 4; ++w) {
             const uint4 bb = xb[16 * w];  // (x0,x4) (x1,x5) (x2,x6) (x3,x7) of word w
 #pragma unroll
@@ -475,8 +483,12 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
                 const uint32_t ub = w == 0 ? r.wb[q].x : w == 1 ? r.wb[q].y
                                                      : w == 2 ? r.wb[q].z : r.wb[q].w;
                 const uint32_t ha = ua >> 8, hb = ub >> 8;
-                mma_16816(acc[q], nib_pair_lo(ua), nib_pair_lo(ub), nib_pair_hi(ua),
-                          nib_pair_hi(ub), bb.x, bb.y);
+                if (w == 0)
+                    mma_16816_z(acc[q], nib_pair_lo(ua), nib_pair_lo(ub), nib_pair_hi(ua),
+                                nib_pair_hi(ub), bb.x, bb.y);
+                else
+                    mma_16816(acc[q], nib_pair_lo(ua), nib_pair_lo(ub), nib_pair_hi(ua),
+                              nib_pair_hi(ub), bb.x, bb.y);
                 mma_16816(acc[q], nib_pair_lo(ha), nib_pair_lo(hb), nib_pair_hi(ha),
                           nib_pair_hi(hb), bb.z, bb.w);
             }
@@ -572,9 +584,6 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
             if constexpr (Fmt::kGroupScale) {
                 float bacc[kNB][4];
 #pragma unroll
-                for (int j = 0; j < kNB; ++j)
-                    bacc[j][0] = bacc[j][1] = bacc[j][2] = bacc[j][3] = 0.f;
-#pragma unroll
                 for (int w = 0; w < 4; ++w) {
                     uint4 bb[kNB];
 #pragma unroll
@@ -582,8 +591,12 @@ __device__ __forceinline__ void mma_item(const MmaItemRegs& r, const uint4* xs, 
                     const uint32_t a0 = nib_pair_lo(ua[w]), a1 = nib_pair_lo(ub[w]);
                     const uint32_t a2 = nib_pair_hi(ua[w]), a3 = nib_pair_hi(ub[w]);
 #pragma unroll
-                    for (int j = 0; j < kNB; ++j)
-                        mma_16816(bacc[j], a0, a1, a2, a3, bb[j].x, bb[j].y);
+                    for (int j = 0; j < kNB; ++j) {
+                        if (w == 0)
+                            mma_16816_z(bacc[j], a0, a1, a2, a3, bb[j].x, bb[j].y);
+                        else
+                            mma_16816(bacc[j], a0, a1, a2, a3, bb[j].x, bb[j].y);
+                    }
                     const uint32_t ha = ua[w] >> 8, hb = ub[w] >> 8;
                     const uint32_t c0 = nib_pair_lo(ha), c1 = nib_pair_lo(hb);
                     const uint32_t c2 = nib_pair_hi(ha), c3 = nib_pair_hi(hb);
