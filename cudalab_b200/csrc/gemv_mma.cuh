@@ -128,15 +128,19 @@ __device__ __forceinline__ void mma_16816_z(float (&d)[4], uint32_t a0, uint32_t
 
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// Nibbles 0 and 4 of w as an exact half2 (q0, q4) ...
+// Nibbles 0 and 4 of w as an exact half2 (q0, q4): the lop3 gives
+// 1024 + (q + 8) per half (exponent of 1024, unit ulp) and one add with an
+// immediate removes the bias ...
 __device__ __forceinline__ uint32_t nib_pair_lo(uint32_t w) {
-    return h2_as_u32(__hfma2(u32_as_h2(lop3_sel_xor_i<0x000F000Fu, 0x64086408u>(w)),
-                             h2_const(kH_one), h2_const(kH_m1032)));
+    return h2_as_u32(__hadd2(u32_as_h2(lop3_sel_xor_i<0x000F000Fu, 0x64086408u>(w)),
+                             h2_const(kH_m1032)));
 }
-// ... and nibbles 1 and 5 as (q1, q5).
+// ... and nibbles 1 and 5 as (q1, q5): they sit at mantissa bits 4..7, so the
+// exponent of 64 (ulp 1/16, i.e. 1 at bit 4) reads them as 64 + (q + 8).
+// Neither form needs a constant register besides the lop3 pattern.
 __device__ __forceinline__ uint32_t nib_pair_hi(uint32_t w) {
-    return h2_as_u32(__hfma2(u32_as_h2(lop3_sel_xor_i<0x00F000F0u, 0x64806480u>(w)),
-                             h2_const(kH_1_16), h2_const(kH_m72)));
+    return h2_as_u32(__hadd2(u32_as_h2(lop3_sel_xor_i<0x00F000F0u, 0x54805480u>(w)),
+                             h2_const(kH_m72)));
 }
 
 // Formats.  kAcc: independent accumulators per item at M = 1 (block q uses
