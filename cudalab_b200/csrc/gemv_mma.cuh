@@ -7,7 +7,7 @@
 // (measured with ncu), which caps the kernel below the HBM roofline.  Here
 // the dequantised fp16 values feed `mma.sync.m16n8k16` (exact fp16 x fp16
 // products, fp32 accumulation), so the multiply-adds leave the issue stream
-// and the dequantisation (one lop3 + one fma.f16x2 per two elements) is
+// and the dequantisation (one lop3 + one add.f16x2 per two elements) is
 // nearly all that remains.  With M > 1 the same dequantised A fragments are
 // reused for every activation row, so the cost per weight barely grows.
 //

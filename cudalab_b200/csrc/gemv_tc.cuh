@@ -10,7 +10,7 @@
 //   * 256 row threads (warps 0-7; warps w and w + 4 share TMEM lanes
 //     32 (w & 3) .. +31 = tile rows, one thread per row and half group): per
 //     group, read their 32 bytes of the row from the stage, dequantise them
-//     exactly (lop3 + fma.f16x2 per two values) and store the 64 fp16 values
+//     exactly (lop3 + add.f16x2 per two values) and store the 64 fp16 values
 //     into a TMEM A buffer with tcgen05.st; stage the group's activations
 //     (16 columns x 128 k, fp16, prefetched one group ahead) into shared
 //     memory; after the group's MMAs, read their 8 accumulator columns back
