@@ -275,7 +275,9 @@ int cl_int4gemv_sharded(const char* variant, const uint8_t* W_shard, const void*
  * scratch is one flag block whatever N, K and M are.  The first call on a
  * device looks up the array's device address; so does the first call after
  * the device's context changed (e.g. after cudaDeviceReset, which loads the
- * library's device code again at a new address).  Every call clears
+ * library's device code again at a new address).  Make that first call on
+ * each device (and the first after a context change) before any stream
+ * capture begins.  Every call clears
  * the block on `stream` before its kernel.  All calls share the one block:
  * calls that overlap on the GPU (other streams, other threads) race and must
  * be serialised by the caller. */
